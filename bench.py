@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""Attention forward throughput on B200: the BASELINE metric, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the box-scale sharded config): B=16, H=32, N=8192,
+D=128, BF16 in / FP32 accumulate, scale 1/sqrt(D). One step = one dense forward
+plus one causal forward over all 512 (batch, head) slabs. With N GPUs (one
+process each, torchrun) the slabs are split into N contiguous ranges and each
+rank runs the same kernel on its own range -- no collective on the data path
+(total work fixed: strong scaling). Time is CUDA events on the launching stream,
+max over ranks. TFLOP/s uses the reference's FLOP count (kernels/v0_unfused.cu:
+118-126: causal pairs N(N+1)/2).
+
+The reference arm (--impl reference) times the reference's own CPU FP64 oracle
+(benchmarks/bench_flash_attention.cu:105-145, compiled from its sources into
+oracle/_ref) on all host cores over a bounded sample of the same workload.
+"""
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "attn fwd TFLOP/s per B200 (D=128, N=8192, dense+causal) and % of BF16 peak"
+CONFIG = {"batch": 16, "heads": 32, "seq_len": 8192, "head_dim": 128}
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), \
+        int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def slab_range(total, rank, world):
+    """Contiguous, near-equal ranges of the flattened batch*heads axis."""
+    base, extra = divmod(total, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            peaks = json.load(fh)
+        return float(peaks["bf16_tflops"]), "measured burst cuBLAS bf16 (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "fa_fwd_kernel_traffic.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_reference_sample(threads, seq_len, head_dim, use_reference=True):
+    """One bounded sample of the workload on the host: `threads` whole slabs, one per thread,
+    alternating dense and causal. Returns (flops, seconds, kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import fa_oracle
+    ref = fa_oracle.load_reference() if use_reference else None
+    kind = "reference" if ref is not None else "port"
+    lib = fa_oracle.load()
+    count = seq_len * head_dim
+    base = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
+    # A private copy of the slab per thread, so no two threads share cache lines.
+    slabs = [tuple(np.copy(x) for x in base) for _ in range(threads)]
+    outs = [np.empty(count, np.float64) for _ in range(threads)]
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+
+    def work(i):
+        causal = i % 2
+        q, k, v = slabs[i]
+        if ref is not None:
+            ref.ref_reference_attention(P(q), P(k), P(v), P(outs[i]), 1, 1, seq_len, head_dim, causal)
+        else:
+            lib.fa_oracle_attention(P(q), P(k), P(v), P(outs[i]), 1, 1, seq_len, head_dim, causal)
+
+    pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    t0 = time.perf_counter()
+    for t in pool:
+        t.start()
+    for t in pool:
+        t.join()
+    seconds = time.perf_counter() - t0
+    flops = sum(fa_oracle.attention_flops(1, 1, seq_len, head_dim, i % 2) for i in range(threads))
+    return flops, seconds, kind
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference_arm(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0   # the CPU reference runs once, on rank 0
+    threads = host_threads()
+    n, d = CONFIG["seq_len"], CONFIG["head_dim"]
+    for _ in range(args.warmup):   # warm-up on a reduced sample: the CPU has nothing to warm
+        cpu_reference_sample(min(threads, 4), 1024, d)
+    flops = secs = 0.0
+    kind = "reference"
+    for _ in range(args.steps):
+        f, s, kind = cpu_reference_sample(threads, n, d)
+        flops += f
+        secs += s
+    value = flops / secs / 1e12
+    sample = (f"{threads} whole (N=8192, D=128) slabs per step, one per host thread, alternating dense/"
+              f"causal, reference_attention (bench_flash_attention.cu:105-145) compiled from the reference "
+              f"sources; warm-up steps used N=1024")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) bf16 (reference generator, seeds 11/22/33)",
+        "impl": "reference",
+        "config": {"workload": "BASELINE config 5 (16,32,8192,128) dense+causal, CPU sample", **CONFIG},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from cuda_fused_attention_b200 import AttentionShape, attention_flops, device_status
+    from cuda_fused_attention_b200 import _lib
+
+    rank, world, local_rank = env_rank()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(values):
+        t = torch.tensor(values, dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    lib = _lib.load()
+    full = AttentionShape(**CONFIG)
+    s0, s1 = slab_range(full.slabs, rank, world)
+    local = s1 - s0
+    n, d = full.seq_len, full.head_dim
+    numel = local * n * d
+    g = torch.Generator(device=device)
+    tensors = []
+    for seed in (11, 22, 33):
+        g.manual_seed(seed * 1000 + rank)
+        tensors.append(torch.randn(numel, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16))
+    q, k, v = tensors
+    o = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+    handle = ctypes.c_void_p(stream.cuda_stream)
+
+    def launch(causal):
+        st = lib.fa_sm100_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), local, 1, n, d,
+                              causal, handle)
+        if st != 0:
+            raise RuntimeError(f"fa_sm100_fwd status {st}")
+
+    flops_dense_local = attention_flops(AttentionShape(local, 1, n, d), False)
+    flops_causal_local = attention_flops(AttentionShape(local, 1, n, d), True)
+    flops_step_total = attention_flops(full, False) + attention_flops(full, True)
+
+    for _ in range(args.warmup):
+        launch(0)
+        launch(1)
+    torch.cuda.synchronize()
+    status, word = device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} ({word:#x}) after warm-up")
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[local_rank] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_id) as clocks:
+        start.record(stream)
+        for a, b, c in ev:
+            a.record(stream)
+            launch(0)
+            b.record(stream)
+            launch(1)
+            c.record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = start.elapsed_time(end)
+    dense_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
+    causal_ms = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
+    status, word = device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} ({word:#x}) after timing")
+    ms_step, dense_ms_max, causal_ms_max = max_over_ranks([total_ms / args.steps, dense_ms, causal_ms])
+    value = flops_step_total / (ms_step * 1e-3) / 1e12
+    peak, peak_src = measured_peak()
+    # Dominant (only) kernel: fa_fwd_kernel<128>; per-launch algorithmic FLOPs / mean launch time.
+    achieved = (flops_dense_local + flops_causal_local) / ((dense_ms + causal_ms) * 1e-3) / 1e12
+    traffic = profile_traffic()
+
+    # ---- end-to-end through the host-buffer C ABI (pinned host memory) --------------------
+    e2e = None
+    if not args.no_e2e:
+        hq = torch.empty(numel, dtype=torch.bfloat16, pin_memory=True)
+        hk = torch.empty_like(hq, pin_memory=True)
+        hv = torch.empty_like(hq, pin_memory=True)
+        ho = torch.empty_like(hq, pin_memory=True)
+        hq.copy_(q)
+        hk.copy_(k)
+        hv.copy_(v)
+
+        def host_step():
+            for causal in (0, 1):
+                st = lib.fa_sm100_fwd_host(hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(),
+                                           local, 1, n, d, causal)
+                if st != 0:
+                    raise RuntimeError(f"fa_sm100_fwd_host status {st}")
+        for _ in range(max(1, args.warmup)):
+            host_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            host_step()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        barrier()
+        (e2e_ms,) = max_over_ranks([e2e_ms])
+        tensor_bytes = full.numel * 2
+        e2e = {"value": flops_step_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": 2 * 3 * tensor_bytes, "d2h_bytes_per_step": 2 * tensor_bytes,
+               "api": "fa_sm100_fwd_host (C ABI, pinned host buffers, H2D+forward+D2H per call; "
+                      "one dense and one causal call per step; bytes summed over ranks)"}
+        lib.fa_sm100_release_staging()
+        del hq, hk, hv, ho
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        f, s, kind = cpu_reference_sample(threads, n, d)
+        cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+               "sample": f"{threads} whole (8192 x 128) slabs, one per host thread, alternating dense/causal, "
+                         f"{s:.1f} s wall"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: torch.randn N(0,1) rounded to bf16, seeds 11/22/33 per rank",
+        "config": {"workload": "BASELINE config 5: (16,32,8192,128), one dense + one causal forward per step",
+                   **CONFIG, "global_batch": CONFIG["batch"], "seq_len": CONFIG["seq_len"],
+                   "parallelism": f"slab-sharded x{world} (batch*heads split, no collective)",
+                   "l2": "inputs larger than L2 (3 GiB of Q/K/V + 1 GiB O per forward)"},
+        "pct_of_bf16_peak": 100.0 * value / world / peak,
+        "dense_tflops": flops_dense_local * world / (dense_ms_max * 1e-3) / 1e12,
+        "causal_tflops": flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_src,
+                     "kernel": "fa_sm100::fa_fwd_kernel<128>",
+                     "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
+                     "traffic_note": None if traffic is None else traffic.get("note")},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps * world,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,68 @@
+"""Build recipe for the sm_100a extension library (in-tree, no JIT cache).
+
+    python -m cuda_fused_attention_b200.build
+
+compiles cuda_fused_attention_b200/csrc/*.cu with nvcc for sm_100a only into
+cuda_fused_attention_b200/lib/libfa_sm100.so. The library exports the C ABI of
+include/fa_sm100.h and the C++ API of include/flash_attention_sm100.h; the CUDA
+runtime is linked statically and the driver is reached only through
+cudaGetDriverEntryPoint, so the .so needs nothing but libc/libstdc++ and the
+NVIDIA driver at run time.
+"""
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+LIB_DIR = os.path.join(PKG_DIR, "lib")
+LIB_PATH = os.path.join(LIB_DIR, "libfa_sm100.so")
+SOURCES = ["fa_sm100.cu", "fa_sm100_host.cu", "fa_sm100_api.cu"]
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path():
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    candidate = os.path.join(cuda_home, "bin", "nvcc")
+    return candidate if os.path.exists(candidate) else (shutil.which("nvcc") or "nvcc")
+
+
+def compile_command(output=LIB_PATH, extra=()):
+    srcs = [os.path.join(CSRC, s) for s in SOURCES]
+    return [nvcc_path(), "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS,
+            "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+            "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+            *extra, *srcs, "-o", output]
+
+
+def needs_build():
+    if not os.path.exists(LIB_PATH):
+        return True
+    lib_time = os.path.getmtime(LIB_PATH)
+    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
+    deps += [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))]
+    return any(os.path.getmtime(d) > lib_time for d in deps)
+
+
+def build(force=False, verbose=True, ptxas_verbose=False):
+    """Compile the library if a source is newer than it; returns its path."""
+    if not force and not needs_build():
+        return LIB_PATH
+    os.makedirs(LIB_DIR, exist_ok=True)
+    extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    cmd = compile_command(extra=extra)
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stdout.write(res.stdout)
+        sys.stderr.write(res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed with exit code {res.returncode}")
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, ptxas_verbose="-v" in sys.argv)

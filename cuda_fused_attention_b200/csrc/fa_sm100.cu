@@ -1,0 +1,749 @@
+// =============================================================================
+// Blackwell (sm_100a) fused attention forward:  O = softmax(Q K^T / sqrt(D) + M) V
+//
+// The hot path of RichterWang/cuda_fused_attention, re-designed for B200. The
+// reference computes it with launch_attention_tensorcore_v3
+// (kernels/v3/v3_tensorcore.cu:418-750): 64 query rows per CTA, Q in
+// registers, cp.async double buffering and warp-level mma.sync. Here:
+//
+//   * One CTA owns 256 query rows of one (batch, head) slab, as two 128-row Q
+//     tiles that ping-pong between two softmax warpgroups.
+//   * QK^T and PV are tcgen05.mma (kind::f16, M=128, N=128 / N=D, BF16 in,
+//     FP32 accumulate) issued by one thread of the MMA warp. S and O live in
+//     tensor memory: S0 | S1 | O0 | O1 = 512 columns at D=128.
+//   * P (bf16) is written back over S in tensor memory and fed to the PV MMA as
+//     its A operand straight from TMEM; P never touches shared memory.
+//   * Q, K and V stream in with TMA (3-D tensor maps over [slabs, N, D], 128-byte
+//     swizzle, zero fill past N) into a K/V ring of mbarrier-guarded stages.
+//   * Softmax is one thread per row: a thread loads its whole S row from TMEM,
+//     so the row max and row sum need no shuffles. exp is ex2 with log2(e)
+//     folded into the scale. O is rescaled in TMEM only when a row max grows.
+//   * Causal: key tiles above the diagonal are never loaded or computed; only
+//     the diagonal tile(s) and a ragged tail tile take the element mask.
+//   * Epilogue: O from TMEM, times 1/l, to bf16, into the (now free) Q tile of
+//     shared memory in the swizzled layout, then one TMA store per 64 columns.
+//
+// Every mbarrier wait is bounded (default one second): on expiry the kernel
+// records the wait site in a device error word, raises a CTA-wide abort flag,
+// drains its own TMA loads and MMAs, frees tensor memory and returns.
+//
+// Warp roles (320 threads):
+//   warps 0-3  softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
+//   warps 4-7  the same for Q tile 1
+//   warp  8    TMEM allocator and MMA issuer (lane 0)
+//   warp  9    TMA producer (lane 0)
+// =============================================================================
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "fa_sm100.h"
+#include "fa_sm100_ptx.cuh"
+
+namespace fa_sm100 {
+
+constexpr int kBlockM = 128;    // query rows per Q tile == TMEM lanes
+constexpr int kBlockN = 128;    // keys per K/V tile
+constexpr int kQTiles = 2;      // Q tiles per CTA
+constexpr int kRowsPerCta = kBlockM * kQTiles;
+constexpr int kThreads = 320;
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
+
+// Wait-site ids recorded in the error word (bits 8..15).
+enum WaitSite : uint32_t {
+    kSiteMmaQ = 1, kSiteMmaK = 2, kSiteMmaV = 3, kSiteMmaP0 = 4, kSiteMmaP1 = 5,
+    kSiteLoadEmpty = 6, kSiteSoftS = 7, kSiteSoftO = 8, kSiteEpilogue = 9, kSiteInjected = 10,
+    kSiteDrain = 11,
+};
+
+template <int D>
+struct Cfg {
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    static constexpr int kSub = D / 64;                       // swizzle blocks per row
+    static constexpr int kTileBytes = kSub * kSubBytes;       // one Q, K or V tile
+    static constexpr int kStages = (D == 128) ? 4 : 8;        // K/V ring slots
+    static constexpr int kQOff = 0;
+    static constexpr int kRingOff = kQTiles * kTileBytes;
+    static constexpr int kBarOff = kRingOff + kStages * kTileBytes;
+    // q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2] o_full[2] epi[2] drain never
+    static constexpr int kBarQFull = 0;
+    static constexpr int kBarKvFull = 2;
+    static constexpr int kBarKvEmpty = 2 + kStages;
+    static constexpr int kBarSFull = 2 + 2 * kStages;
+    static constexpr int kBarPFull = kBarSFull + 2;
+    static constexpr int kBarOFull = kBarPFull + 2;
+    static constexpr int kBarEpi = kBarOFull + 2;
+    static constexpr int kBarDrain = kBarEpi + 2;
+    static constexpr int kBarNever = kBarDrain + 1;
+    static constexpr int kNumBars = kBarNever + 1;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;   // tmem base (u32), abort flag (u32)
+    static constexpr int kSmemUsed = kMiscOff + 16;
+    static constexpr int kSmemBytes = kSmemUsed + 1024;       // slack for 1024-byte alignment
+    static constexpr uint32_t kColS0 = 0;
+    static constexpr uint32_t kColS1 = kBlockN;
+    static constexpr uint32_t kColO0 = 2 * kBlockN;
+    static constexpr uint32_t kColO1 = 2 * kBlockN + D;
+    static constexpr uint32_t kIdescQK = make_idesc_bf16(kBlockM, kBlockN, false);
+    static constexpr uint32_t kIdescPV = make_idesc_bf16(kBlockM, D, true);
+    static_assert(kColO1 + D <= kTmemCols, "TMEM budget");
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct Params {
+    int seq_len;
+    int num_pairs;              // ceil(seq_len / 256): CTAs per slab
+    long long slab_begin;       // first slab of this launch in the full tensor
+    float scale_log2;           // default_scale(D) * log2(e)
+    int causal;
+    int inject_stall;           // test only: the MMA warp waits on a barrier nothing arrives on
+    unsigned long long timeout_ns;
+};
+
+// Device error word of this module instance (one per device). Bit 0: some wait
+// timed out; bits 8..15: the site of the first recorded timeout.
+__device__ unsigned int g_fa_error_word;
+
+__device__ __forceinline__ void record_timeout(volatile uint32_t* abort_flag, uint32_t site)
+{
+    *abort_flag = 1u;
+    atomicCAS(&g_fa_error_word, 0u, 1u | (site << 8));
+    atomicOr(&g_fa_error_word, 1u);
+}
+
+// Bounded wait on an mbarrier phase. Returns false when the CTA is aborting or
+// the wait ran past timeout_ns (which raises the abort itself).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                             unsigned long long timeout_ns, uint32_t site)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 7u) == 0u) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - start > timeout_ns) {
+                record_timeout(abort_flag, site);
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait used on the abort path: ignores the abort flag, still gives up
+// after timeout_ns.
+__device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, unsigned long long timeout_ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 7u) == 0u && global_timer_ns() - start > timeout_ns) {
+            atomicOr(&g_fa_error_word, 1u);
+            return false;
+        }
+    }
+}
+
+// QK^T for one Q tile against one K tile: D/16 MMAs of M=128, N=128, K=16.
+// Both operands K-major in 128-byte swizzled 64-element blocks; the K step
+// advances 32 bytes inside a block, then moves to the next block.
+template <int D>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_saddr, uint32_t k_saddr)
+{
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = static_cast<uint32_t>((kk >> 2) * kSubBytes + (kk & 3) * 32);
+        const uint64_t a = make_smem_desc(q_saddr + off, 16, 1024);
+        const uint64_t b = make_smem_desc(k_saddr + off, 16, 1024);
+        umma_ss(d_tmem, a, b, Cfg<D>::kIdescQK, kk > 0 ? 1u : 0u);
+    }
+}
+
+// O (+)= P V: 8 MMAs of M=128, N=D, K=16 keys. P comes from TMEM (16 keys =
+// 8 columns of packed bf16 pairs); V is MN-major: 64-column blocks kSubBytes
+// apart (LBO), 8-key row groups 1024 bytes apart (SBO).
+template <int D>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_saddr, bool accumulate)
+{
+#pragma unroll
+    for (int kk = 0; kk < kBlockN / 16; ++kk) {
+        const uint64_t b = make_smem_desc(v_saddr + static_cast<uint32_t>(kk * 16 * 128), kSubBytes, 1024);
+        umma_ts(d_tmem, p_tmem + static_cast<uint32_t>(kk * 8), b, Cfg<D>::kIdescPV,
+                (accumulate || kk > 0) ? 1u : 0u);
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+              const Params p)
+{
+    using C = Cfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment: the 128-byte swizzle pattern repeats every 8 rows.
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_addr);
+
+    const uint32_t sq = base + C::kQOff;
+    const uint32_t ring = base + C::kRingOff;
+    const uint32_t bars = base + C::kBarOff;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMiscOff + 4);
+    auto bar = [&](int index) -> uint32_t { return bars + static_cast<uint32_t>(index) * 8u; };
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    // ---- work item: slab-major, heaviest causal tiles of a slab first --------
+    const long long block = blockIdx.x;
+    const long long slab_local = block / p.num_pairs;
+    int pair = static_cast<int>(block - slab_local * p.num_pairs);
+    if (p.causal) pair = p.num_pairs - 1 - pair;
+    const int slab = static_cast<int>(p.slab_begin + slab_local);
+    const int q_row0 = pair * kRowsPerCta;
+    const int n = p.seq_len;
+    const int kv_tiles_all = (n + kBlockN - 1) / kBlockN;
+    const int n_kv = p.causal ? min(kv_tiles_all, 2 * pair + 2) : kv_tiles_all;
+
+    // ---- set-up ---------------------------------------------------------------
+    if (threadIdx.x == 0) {
+        mbar_init(bar(C::kBarQFull + 0), 1);
+        mbar_init(bar(C::kBarQFull + 1), 1);
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(bar(C::kBarKvFull + s), 1);
+            mbar_init(bar(C::kBarKvEmpty + s), 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(bar(C::kBarSFull + t), 1);
+            mbar_init(bar(C::kBarPFull + t), kBlockM);
+            mbar_init(bar(C::kBarOFull + t), 1);
+            mbar_init(bar(C::kBarEpi + t), kBlockM);
+        }
+        mbar_init(bar(C::kBarDrain), 1);
+        mbar_init(bar(C::kBarNever), 1);
+        *abort_flag = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const unsigned long long timeout = p.timeout_ns;
+
+    if (warp == kLoadWarp) {
+        // ======================= TMA producer ==================================
+        if (lane == 0) {
+            tma_prefetch_map(&tm_q);
+            tma_prefetch_map(&tm_k);
+            tma_prefetch_map(&tm_v);
+            tma_prefetch_map(&tm_o);
+            for (int t = 0; t < 2; ++t) {
+                mbar_arrive_expect_tx(bar(C::kBarQFull + t), C::kTileBytes);
+#pragma unroll
+                for (int s = 0; s < C::kSub; ++s)
+                    tma_load_3d(sq + t * C::kTileBytes + s * kSubBytes, &tm_q, bar(C::kBarQFull + t), s * 64,
+                                q_row0 + t * kBlockM, slab);
+            }
+            bool ok = true;
+            int issued = 0;
+            for (int i = 0; i < 2 * n_kv; ++i) {
+                const int slot = i % C::kStages;
+                const int use = i / C::kStages;
+                if (use > 0 && !wait_bounded(bar(C::kBarKvEmpty + slot), (use - 1) & 1, abort_flag, timeout,
+                                             kSiteLoadEmpty)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(bar(C::kBarKvFull + slot), C::kTileBytes);
+                const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+                const int key0 = (i >> 1) * kBlockN;
+#pragma unroll
+                for (int s = 0; s < C::kSub; ++s)
+                    tma_load_3d(ring + slot * C::kTileBytes + s * kSubBytes, map, bar(C::kBarKvFull + slot),
+                                s * 64, key0, slab);
+                ++issued;
+            }
+            if (!ok) {
+                // Abort: let every copy this CTA started land before shared memory goes away.
+                wait_drain(bar(C::kBarQFull + 0), 0, timeout);
+                wait_drain(bar(C::kBarQFull + 1), 0, timeout);
+                for (int i = max(0, issued - C::kStages); i < issued; ++i)
+                    wait_drain(bar(C::kBarKvFull + i % C::kStages), (i / C::kStages) & 1, timeout);
+            }
+        }
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        // ======================= MMA issuer ====================================
+        if (lane == 0) {
+            const uint32_t t_s0 = tmem_base + C::kColS0;
+            const uint32_t t_s1 = tmem_base + C::kColS1;
+            const uint32_t t_o0 = tmem_base + C::kColO0;
+            const uint32_t t_o1 = tmem_base + C::kColO1;
+            const uint32_t sq0 = sq;
+            const uint32_t sq1 = sq + C::kTileBytes;
+            auto slot_addr = [&](int i) -> uint32_t { return ring + (i % C::kStages) * C::kTileBytes; };
+            auto full_bar = [&](int i) -> uint32_t { return bar(C::kBarKvFull + i % C::kStages); };
+            auto empty_bar = [&](int i) -> uint32_t { return bar(C::kBarKvEmpty + i % C::kStages); };
+            auto full_par = [&](int i) -> uint32_t { return static_cast<uint32_t>((i / C::kStages) & 1); };
+
+            bool ok = wait_bounded(bar(C::kBarQFull + 0), 0, abort_flag, timeout, kSiteMmaQ) &&
+                      wait_bounded(bar(C::kBarQFull + 1), 0, abort_flag, timeout, kSiteMmaQ);
+            if (ok && p.inject_stall) ok = wait_bounded(bar(C::kBarNever), 0, abort_flag, timeout, kSiteInjected);
+            if (ok) ok = wait_bounded(full_bar(0), full_par(0), abort_flag, timeout, kSiteMmaK);
+            if (ok) {
+                tc_fence_after();
+                issue_qk<D>(t_s0, sq0, slot_addr(0));
+                umma_commit(bar(C::kBarSFull + 0));
+                issue_qk<D>(t_s1, sq1, slot_addr(0));
+                umma_commit(bar(C::kBarSFull + 1));
+                umma_commit(empty_bar(0));
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const int vi = 2 * j + 1;      // ring index of V_j
+                const int ki = 2 * j + 2;      // ring index of K_{j+1}
+                const bool more = j + 1 < n_kv;
+                const bool last = !more;
+                if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
+                if (!wait_bounded(bar(C::kBarPFull + 0), j & 1, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv<D>(t_o0, t_s0, slot_addr(vi), j > 0);
+                if (last) umma_commit(bar(C::kBarOFull + 0));
+                if (more) {
+                    if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_qk<D>(t_s0, sq0, slot_addr(ki));
+                    umma_commit(bar(C::kBarSFull + 0));
+                }
+                if (!wait_bounded(bar(C::kBarPFull + 1), j & 1, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv<D>(t_o1, t_s1, slot_addr(vi), j > 0);
+                umma_commit(empty_bar(vi));
+                if (last) umma_commit(bar(C::kBarOFull + 1));
+                if (more) {
+                    issue_qk<D>(t_s1, sq1, slot_addr(ki));
+                    umma_commit(bar(C::kBarSFull + 1));
+                    umma_commit(empty_bar(ki));
+                }
+            }
+            // Every MMA issued above must finish before tensor memory is released.
+            umma_commit(bar(C::kBarDrain));
+            wait_drain(bar(C::kBarDrain), 0, timeout);
+        }
+        __syncwarp();
+    } else {
+        // ======================= softmax / correction / epilogue ================
+        const int t = warp / 4;                    // Q tile of this warpgroup
+        const int quarter = warp % 4;              // TMEM lane quarter of this warp
+        const int r = quarter * 32 + lane;         // row within the Q tile == TMEM lane
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t t_s = lane_base + (t == 0 ? C::kColS0 : C::kColS1);
+        const uint32_t t_o = lane_base + (t == 0 ? C::kColO0 : C::kColO1);
+        const int row = q_row0 + t * kBlockM + r;            // query index in the slab
+        const int limit = p.causal ? min(row, n - 1) : n - 1;  // last key this row attends to
+        const int diag_tile = 2 * pair + t;                  // first key tile that needs the causal mask
+        const float sl2 = p.scale_log2;
+
+        float row_max = -INFINITY;   // running max of raw scores
+        float row_sum = 0.0f;        // running sum of exp2((s - max) * sl2), fp32 before rounding
+        bool ok = true;
+
+        for (int j = 0; j < n_kv; ++j) {
+            ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarSFull + t), j & 1, abort_flag, timeout, kSiteSoftS));
+            if (!ok) break;
+            tc_fence_after();
+
+            uint32_t s[4][32];
+            tmem_ld32(t_s + 0, s[0]);
+            tmem_ld32(t_s + 32, s[1]);
+            tmem_ld32(t_s + 64, s[2]);
+            tmem_ld32(t_s + 96, s[3]);
+            tmem_wait_ld();
+            reg_fence32(s[0]);
+            reg_fence32(s[1]);
+            reg_fence32(s[2]);
+            reg_fence32(s[3]);
+
+            const bool mask_tile = (p.causal && j >= diag_tile) || ((j + 1) * kBlockN > n);
+            if (mask_tile) {
+                const int key0 = j * kBlockN;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (key0 + c * 32 + i > limit) s[c][i] = __float_as_uint(-INFINITY);
+            }
+
+            float m0 = row_max, m1 = row_max, m2 = row_max, m3 = row_max;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                m0 = fmaxf(m0, __uint_as_float(s[0][i]));
+                m1 = fmaxf(m1, __uint_as_float(s[1][i]));
+                m2 = fmaxf(m2, __uint_as_float(s[2][i]));
+                m3 = fmaxf(m3, __uint_as_float(s[3][i]));
+            }
+            const float m_new = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+            const float m_base = (m_new == -INFINITY) ? 0.0f : m_new * sl2;
+            const float alpha = ex2_approx(row_max * sl2 - m_base);
+
+            float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i]), sl2, -m_base));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i + 1]), sl2, -m_base));
+                    sum0 += p0;
+                    sum1 += p1;
+                    packed[i] = pack_bf16x2(p0, p1);
+                }
+                tmem_st16(t_s + static_cast<uint32_t>(c * 16), packed);
+            }
+            row_sum = row_sum * alpha + (sum0 + sum1);
+
+            // O correction: only when some row of this warp raised its max, and
+            // never before the first PV has written O.
+            if (j > 0 && __any_sync(0xffffffffu, m_new > row_max)) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
+                    tmem_wait_ld();
+                    reg_fence32(o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(t_o + static_cast<uint32_t>(c * 32), o);
+                }
+            }
+            row_max = m_new;
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(C::kBarPFull + t));
+        }
+
+        // ---- epilogue ---------------------------------------------------------
+        if (ok) ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarOFull + t), 0, abort_flag, timeout, kSiteSoftO));
+        if (ok) {
+            tc_fence_after();
+            const float inv = row_sum > 0.0f ? 1.0f / row_sum : 0.0f;
+            // The last QK MMA of this tile has completed, so its Q tile is free:
+            // stage O there in the 128-byte swizzled layout the store map expects.
+            const uint32_t stage = sq + static_cast<uint32_t>(t * C::kTileBytes);
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
+                tmem_wait_ld();
+                reg_fence32(o);
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+                const int sub = (c * 32) / 64;
+                const int chunk0 = ((c * 32) % 64) / 8;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int phys = (chunk0 + q) ^ (r & 7);
+                    const uint32_t addr = stage + static_cast<uint32_t>(sub * kSubBytes + r * 128 + phys * 16);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+                                 :: "r"(addr), "r"(packed[4 * q]), "r"(packed[4 * q + 1]),
+                                    "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3]) : "memory");
+                }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(bar(C::kBarEpi + t));
+            if (r == 0) {
+                if (wait_bounded(bar(C::kBarEpi + t), 0, abort_flag, timeout, kSiteEpilogue)) {
+#pragma unroll
+                    for (int s = 0; s < C::kSub; ++s)
+                        tma_store_3d(&tm_o, stage + static_cast<uint32_t>(s * kSubBytes), s * 64,
+                                     q_row0 + t * kBlockM, slab);
+                    tma_store_commit();
+                    tma_store_wait_all();
+                }
+            }
+        }
+        tc_fence_before();
+    }
+
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+}  // namespace fa_sm100
+
+// =============================================================================
+// Host side
+// =============================================================================
+namespace {
+
+using namespace fa_sm100;
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;   // one second
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult query{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) == cudaSuccess &&
+            query == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// Per-device one-time state: architecture check and the shared-memory opt-in.
+struct DeviceState {
+    std::once_flag once;
+    int status = FA_STATUS_OK;
+};
+DeviceState g_devices[kMaxDevices];
+
+int prepare_device(int device)
+{
+    if (device < 0 || device >= kMaxDevices) return FA_STATUS_INVALID_ARGUMENT;
+    DeviceState& state = g_devices[device];
+    std::call_once(state.once, [&]() {
+        int major = 0;
+        cudaError_t err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+        if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
+        if (major != 10) { state.status = FA_STATUS_NO_SM100; return; }
+        err = cudaFuncSetAttribute(fa_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::kSmemBytes);
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(fa_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg<128>::kSmemBytes);
+        if (err != cudaSuccess) state.status = static_cast<int>(err);
+    });
+    return state.status;
+}
+
+// 3-D view [slabs, seq_len, head_dim] of a contiguous bf16 tensor; box = 64
+// columns (128 bytes, the swizzle span) x 128 rows x 1 slab; rows past seq_len
+// read as zero and are clipped on store.
+int make_map(CUtensorMap* map, const void* ptr, long long slabs, int seq_len, int head_dim)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return FA_STATUS_DRIVER_ENTRY;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq_len),
+                                static_cast<cuuint64_t>(slabs)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2u,
+                                   static_cast<cuuint64_t>(seq_len) * static_cast<cuuint64_t>(head_dim) * 2u};
+    const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(kBlockM), 1u};
+    const cuuint32_t elem_strides[3] = {1u, 1u, 1u};
+    const CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                            elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return res == CUDA_SUCCESS ? FA_STATUS_OK : FA_STATUS_TENSOR_MAP;
+}
+
+int validate(const void* q, const void* k, const void* v, const void* o, int batch, int heads, int seq_len,
+             int head_dim, long long slab_begin, long long slab_end)
+{
+    if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return FA_STATUS_INVALID_ARGUMENT;
+    if (batch <= 0 || heads <= 0 || seq_len <= 0) return FA_STATUS_INVALID_ARGUMENT;
+    if (head_dim != 64 && head_dim != 128) return FA_STATUS_UNSUPPORTED;
+    const long long slabs = static_cast<long long>(batch) * heads;
+    if (slabs > INT_MAX) return FA_STATUS_INVALID_ARGUMENT;
+    if (seq_len > (1 << 30)) return FA_STATUS_INVALID_ARGUMENT;
+    if (slab_begin < 0 || slab_end > slabs || slab_begin > slab_end) return FA_STATUS_INVALID_ARGUMENT;
+    const uintptr_t any = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o);
+    if (any & 15u) return FA_STATUS_MISALIGNED;
+    return FA_STATUS_OK;
+}
+
+template <int D>
+int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+           const Params& params, long long slabs, cudaStream_t stream)
+{
+    const long long blocks = slabs * params.num_pairs;
+    if (blocks <= 0) return FA_STATUS_OK;
+    if (blocks > INT_MAX) return FA_STATUS_INVALID_ARGUMENT;
+    fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+    return static_cast<int>(cudaGetLastError());
+}
+
+int forward(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len, int head_dim,
+            int causal, long long slab_begin, long long slab_end, void* stream, int inject_stall,
+            unsigned long long timeout_ns)
+{
+    int status = validate(q, k, v, o, batch, heads, seq_len, head_dim, slab_begin, slab_end);
+    if (status != FA_STATUS_OK) return status;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return static_cast<int>(err);
+    status = prepare_device(device);
+    if (status != FA_STATUS_OK) return status;
+    if (slab_end == slab_begin) return FA_STATUS_OK;
+
+    const long long slabs = static_cast<long long>(batch) * heads;
+    CUtensorMap mq, mk, mv, mo;
+    if ((status = make_map(&mq, q, slabs, seq_len, head_dim)) != FA_STATUS_OK) return status;
+    if ((status = make_map(&mk, k, slabs, seq_len, head_dim)) != FA_STATUS_OK) return status;
+    if ((status = make_map(&mv, v, slabs, seq_len, head_dim)) != FA_STATUS_OK) return status;
+    if ((status = make_map(&mo, o, slabs, seq_len, head_dim)) != FA_STATUS_OK) return status;
+
+    Params params{};
+    params.seq_len = seq_len;
+    params.num_pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
+    params.slab_begin = slab_begin;
+    params.scale_log2 = fa_default_scale(head_dim) * 1.4426950408889634f;
+    params.causal = causal ? 1 : 0;
+    params.inject_stall = inject_stall;
+    params.timeout_ns = timeout_ns;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const long long count = slab_end - slab_begin;
+    return head_dim == 64 ? launch<64>(mq, mk, mv, mo, params, count, s)
+                          : launch<128>(mq, mk, mv, mo, params, count, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_sm100_fwd(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len,
+                 int head_dim, int causal, void* stream)
+{
+    const long long slabs = (batch > 0 && heads > 0) ? static_cast<long long>(batch) * heads : 0;
+    return forward(q, k, v, o, batch, heads, seq_len, head_dim, causal, 0, slabs, stream, 0, kDefaultTimeoutNs);
+}
+
+int fa_sm100_fwd_slabs(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len,
+                       int head_dim, int causal, long long slab_begin, long long slab_end, void* stream)
+{
+    return forward(q, k, v, o, batch, heads, seq_len, head_dim, causal, slab_begin, slab_end, stream, 0,
+                   kDefaultTimeoutNs);
+}
+
+int fa_sm100_fwd_inject_stall(const void* q, const void* k, const void* v, void* o, int batch, int heads,
+                              int seq_len, int head_dim, int causal, unsigned long long timeout_ns, void* stream)
+{
+    if (timeout_ns == 0 || timeout_ns > kDefaultTimeoutNs) return FA_STATUS_INVALID_ARGUMENT;
+    const long long slabs = (batch > 0 && heads > 0) ? static_cast<long long>(batch) * heads : 0;
+    return forward(q, k, v, o, batch, heads, seq_len, head_dim, causal, 0, slabs, stream, 1, timeout_ns);
+}
+
+int fa_sm100_supported(int head_dim) { return (head_dim == 64 || head_dim == 128) ? 1 : 0; }
+
+float fa_default_scale(int head_dim) { return 1.0f / std::sqrt(static_cast<float>(head_dim)); }
+
+double fa_attention_flops(int batch, int heads, int seq_len, int head_dim, int causal)
+{
+    const double n = static_cast<double>(seq_len);
+    const double pairs = causal ? n * (n + 1.0) / 2.0 : n * n;
+    return 4.0 * pairs * static_cast<double>(head_dim) * static_cast<double>(batch) * static_cast<double>(heads);
+}
+
+double fa_sm100_min_bytes(int batch, int heads, int seq_len, int head_dim)
+{
+    return 4.0 * static_cast<double>(batch) * heads * seq_len * head_dim * 2.0;
+}
+
+double fa_sm100_hbm_bytes(int batch, int heads, int seq_len, int head_dim, int causal)
+{
+    const double element = 2.0;
+    const double slabs = static_cast<double>(batch) * heads;
+    double bytes = 2.0 * slabs * seq_len * head_dim * element;     // Q read once, O written once
+    const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
+    const int kv_all = (seq_len + kBlockN - 1) / kBlockN;
+    double kv_tiles = 0.0;
+    for (int pair = 0; pair < pairs; ++pair)
+        kv_tiles += causal ? (2 * pair + 2 < kv_all ? 2 * pair + 2 : kv_all) : kv_all;
+    bytes += 2.0 * slabs * kv_tiles * kBlockN * head_dim * element;   // a K and a V tile per visit
+    return bytes;
+}
+
+int fa_sm100_query(int head_dim, FaTilingInfo* info)
+{
+    if (info == nullptr) return FA_STATUS_INVALID_ARGUMENT;
+    std::memset(info, 0, sizeof(*info));
+    info->supported = fa_sm100_supported(head_dim);
+    if (!info->supported) return FA_STATUS_OK;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return static_cast<int>(err);
+    const int status = prepare_device(device);
+    if (status != FA_STATUS_OK) return status;
+    const void* func = head_dim == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<64>)
+                                      : reinterpret_cast<const void*>(fa_fwd_kernel<128>);
+    const int dynamic_bytes = head_dim == 64 ? Cfg<64>::kSmemBytes : Cfg<128>::kSmemBytes;
+    cudaFuncAttributes attributes{};
+    if ((err = cudaFuncGetAttributes(&attributes, func)) != cudaSuccess) return static_cast<int>(err);
+    info->block_size = kThreads;
+    info->tile_kv = kBlockN;
+    info->rows_per_block = kRowsPerCta;
+    info->shared_bytes_per_block = static_cast<int>(attributes.sharedSizeBytes) + dynamic_bytes;
+    info->registers_per_thread = attributes.numRegs;
+    info->local_bytes_per_thread = static_cast<int>(attributes.localSizeBytes);
+    int blocks = 0;
+    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, func, kThreads, dynamic_bytes)) != cudaSuccess)
+        return static_cast<int>(err);
+    info->max_blocks_per_sm = blocks;
+    int shared_per_sm = 0;
+    cudaDeviceGetAttribute(&shared_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+    info->device_shared_bytes_per_sm = shared_per_sm;
+    info->shared_limited_blocks_per_sm =
+        info->shared_bytes_per_block > 0 ? shared_per_sm / info->shared_bytes_per_block : 0;
+    return FA_STATUS_OK;
+}
+
+int fa_sm100_device_status(unsigned int* detail)
+{
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return static_cast<int>(err);
+    unsigned int word = 0;
+    err = cudaMemcpyFromSymbol(&word, g_fa_error_word, sizeof(word));
+    if (err != cudaSuccess) return static_cast<int>(err);
+    const unsigned int zero = 0;
+    err = cudaMemcpyToSymbol(g_fa_error_word, &zero, sizeof(zero));
+    if (err != cudaSuccess) return static_cast<int>(err);
+    if (detail != nullptr) *detail = word;
+    return word ? FA_STATUS_DEVICE_TIMEOUT : FA_STATUS_OK;
+}
+
+const char* fa_sm100_status_string(int status)
+{
+    switch (status) {
+        case FA_STATUS_OK: return "ok";
+        case FA_STATUS_INVALID_ARGUMENT: return "invalid argument";
+        case FA_STATUS_UNSUPPORTED: return "unsupported head_dim (64 or 128)";
+        case FA_STATUS_MISALIGNED: return "tensor base not 16-byte aligned";
+        case FA_STATUS_NO_SM100: return "device is not sm_100 (B200)";
+        case FA_STATUS_DRIVER_ENTRY: return "cuTensorMapEncodeTiled unavailable";
+        case FA_STATUS_TENSOR_MAP: return "tensor map encoding failed";
+        case FA_STATUS_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case FA_STATUS_HOST_ALLOC: return "staging allocation failed";
+        default: break;
+    }
+    if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));
+    return "unknown status";
+}
+
+}  // extern "C"
