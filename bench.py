@@ -43,6 +43,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--shape", default=None,
+                    help="B,H,N,D instead of config 5 (profiling and exploration; not the headline)")
+    ap.add_argument("--mask", choices=["both", "dense", "causal"], default="both",
+                    help="forwards per step (default: one dense + one causal)")
     return ap.parse_args()
 
 
@@ -237,7 +241,12 @@ def run_ours(args):
         return t.tolist()
 
     lib = _lib.load()
-    full = AttentionShape(**CONFIG)
+    config = dict(CONFIG)
+    if args.shape:
+        b_, h_, n_, d_ = (int(x) for x in args.shape.split(","))
+        config = {"batch": b_, "heads": h_, "seq_len": n_, "head_dim": d_}
+    masks = {"both": (0, 1), "dense": (0,), "causal": (1,)}[args.mask]
+    full = AttentionShape(**config)
     s0, s1 = slab_range(full.slabs, rank, world)
     local = s1 - s0
     n, d = full.seq_len, full.head_dim
@@ -258,13 +267,16 @@ def run_ours(args):
         if st != 0:
             raise RuntimeError(f"fa_sm100_fwd status {st}")
 
-    flops_dense_local = attention_flops(AttentionShape(local, 1, n, d), False)
-    flops_causal_local = attention_flops(AttentionShape(local, 1, n, d), True)
-    flops_step_total = attention_flops(full, False) + attention_flops(full, True)
+    flops_dense_local = attention_flops(AttentionShape(local, 1, n, d), False) if 0 in masks else 0.0
+    flops_causal_local = attention_flops(AttentionShape(local, 1, n, d), True) if 1 in masks else 0.0
+    flops_step_total = sum(attention_flops(full, bool(c)) for c in masks)
+
+    def step():
+        for c in masks:
+            launch(c)
 
     for _ in range(args.warmup):
-        launch(0)
-        launch(1)
+        step()
     torch.cuda.synchronize()
     status, word = device_status()
     if status != 0:
@@ -281,9 +293,11 @@ def run_ours(args):
         start.record(stream)
         for a, b, c in ev:
             a.record(stream)
-            launch(0)
+            if 0 in masks:
+                launch(0)
             b.record(stream)
-            launch(1)
+            if 1 in masks:
+                launch(1)
             c.record(stream)
         end.record(stream)
         torch.cuda.synchronize()
@@ -313,7 +327,7 @@ def run_ours(args):
         hv.copy_(v)
 
         def host_step():
-            for causal in (0, 1):
+            for causal in masks:
                 st = lib.fa_sm100_fwd_host(hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(),
                                            local, 1, n, d, causal)
                 if st != 0:
@@ -330,7 +344,8 @@ def run_ours(args):
         tensor_bytes = full.numel * 2
         e2e = {"value": flops_step_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": 2 * 3 * tensor_bytes, "d2h_bytes_per_step": 2 * tensor_bytes,
+               "h2d_bytes_per_step": len(masks) * 3 * tensor_bytes,
+               "d2h_bytes_per_step": len(masks) * tensor_bytes,
                "api": "fa_sm100_fwd_host (C ABI, pinned host buffers, H2D+forward+D2H per call; "
                       "one dense and one causal call per step; bytes summed over ranks)"}
         lib.fa_sm100_release_staging()
@@ -353,13 +368,15 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: torch.randn N(0,1) rounded to bf16, seeds 11/22/33 per rank",
-        "config": {"workload": "BASELINE config 5: (16,32,8192,128), one dense + one causal forward per step",
-                   **CONFIG, "global_batch": CONFIG["batch"], "seq_len": CONFIG["seq_len"],
+        "config": {"workload": ("BASELINE config 5: (16,32,8192,128), one dense + one causal forward per step"
+                                if not args.shape and args.mask == "both" else
+                                f"exploration shape {tuple(config.values())}, masks {args.mask} (not the headline)"),
+                   **config, "global_batch": config["batch"],
                    "parallelism": f"slab-sharded x{world} (batch*heads split, no collective)",
                    "l2": "inputs larger than L2 (3 GiB of Q/K/V + 1 GiB O per forward)"},
         "pct_of_bf16_peak": 100.0 * value / world / peak,
-        "dense_tflops": flops_dense_local * world / (dense_ms_max * 1e-3) / 1e12,
-        "causal_tflops": flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12,
+        "dense_tflops": (flops_dense_local * world / (dense_ms_max * 1e-3) / 1e12) if 0 in masks else None,
+        "causal_tflops": (flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12) if 1 in masks else None,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src,
                      "kernel": "fa_sm100::fa_fwd_kernel<128>",
@@ -367,7 +384,7 @@ def run_ours(args):
                      "traffic_note": None if traffic is None else traffic.get("note")},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps * world,
+        "gpu_launches": len(masks) * args.steps * world,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -230,28 +230,37 @@ def test_host_entry_matches_device_entry(oracle, cuda_device):
 
 
 def test_against_reference_v3_built_for_sm100(oracle, cuda_device):
-    """The reference's own v3 kernel (kernels/v3/v3_tensorcore.cu) built for sm_100a is the second
-    opinion: both kernels pass the same gate on the same inputs, and agree to within 2 ULP of each
-    other's row scale."""
+    """The reference's own v3 kernel (kernels/v3/v3_tensorcore.cu) built for sm_100a, run on the
+    same inputs, as a second opinion. Ours must pass the gate on every shape. v3 is held to the
+    gate only on the shape its own accuracy suite validates, (1,2,256,D)
+    (bench_flash_attention.cu:514-530); elsewhere its error is reported, not asserted: built for
+    sm_100a it exceeds the gate at longer sequences (e.g. (2,8,2048,64) causal)."""
     import torch
     ref_lib = oracle.load_reference()
     if ref_lib is None:
         pytest.skip("oracle/_ref/libfa_ref.so was not built (needs the reference tree at build time)")
     from cuda_fused_attention_b200 import AttentionShape
-    for (b, h, n, d, causal) in [(1, 2, 256, 64, 0), (1, 2, 256, 128, 1), (2, 8, 2048, 64, 1), (1, 4, 1000, 128, 0)]:
+    report = []
+    for (b, h, n, d, causal) in [(1, 2, 256, 64, 0), (1, 2, 256, 64, 1), (1, 2, 256, 128, 0), (1, 2, 256, 128, 1),
+                                 (1, 2, 512, 64, 1), (1, 2, 1024, 128, 1), (2, 8, 2048, 64, 0),
+                                 (2, 8, 2048, 64, 1), (1, 4, 1000, 128, 0)]:
         q, k, v = oracle.make_inputs(b, h, n, d)
         ref = oracle.attention(q, k, v, b, h, n, d, causal)
         mine = run_kernel(q, k, v, AttentionShape(b, h, n, d), causal, cuda_device)
         dq, dk, dv = _to_dev(q, cuda_device), _to_dev(k, cuda_device), _to_dev(v, cuda_device)
         do = _poisoned_like(dq)
+        torch.cuda.synchronize()
         rc = ref_lib.ref_launch_tensorcore_v3(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(),
                                               b, h, n, d, causal, None)
         assert rc == 0
         torch.cuda.synchronize()
-        theirs = _to_host_bits(do)
+        theirs = oracle.compare(_to_host_bits(do), ref, d, TOL)
         a_mine = assert_parity(mine, ref, d, "sm100")
-        a_theirs = assert_parity(theirs, ref, d, "v3")
-        assert a_mine["ulp"] <= max(TOL, a_theirs["ulp"])
+        report.append(f"({b},{h},{n},{d}) causal={causal}: sm100 {a_mine['ulp']:.2f} ulp, "
+                      f"v3@sm_100a {theirs['ulp']:.2f} ulp")
+        if (b, h, n) == (1, 2, 256):
+            assert theirs["passed"], ("v3", theirs)
+    print("\n".join(report))
 
 
 def test_config1_against_reference_unfused(oracle, cuda_device):
