@@ -19,6 +19,7 @@ STATUS_DRIVER_ENTRY = 1005
 STATUS_TENSOR_MAP = 1006
 STATUS_DEVICE_TIMEOUT = 1007
 STATUS_HOST_ALLOC = 1008
+STATUS_BUILD_MISMATCH = 1009
 
 #: Every symbol include/fa_sm100.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p

@@ -27,11 +27,14 @@
 // records the wait site in a device error word, raises a CTA-wide abort flag,
 // drains its own TMA loads and MMAs, frees tensor memory and returns.
 //
-// Warp roles (320 threads):
-//   warps 0-3  softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
-//   warps 4-7  the same for Q tile 1
-//   warp  8    TMEM allocator and MMA issuer (lane 0)
-//   warp  9    TMA producer (lane 0)
+// Warp roles (384 threads = 3 warpgroups):
+//   warps 0-3   softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
+//   warps 4-7   the same for Q tile 1
+//   warp  8     TMEM allocator and MMA issuer (lane 0)
+//   warp  9     TMA producer (lane 0)
+//   warps 10-11 idle (they complete the third warpgroup for the register split)
+// Registers: launched at 168 per thread; the softmax warpgroups grow to 216 and the
+// third warpgroup shrinks to 72 (setmaxnreg), 2*128*216 + 128*72 = 384*168.
 // =============================================================================
 
 #include <cuda.h>
@@ -53,9 +56,23 @@ constexpr int kBlockM = 128;    // query rows per Q tile == TMEM lanes
 constexpr int kBlockN = 128;    // keys per K/V tile
 constexpr int kQTiles = 2;      // Q tiles per CTA
 constexpr int kRowsPerCta = kBlockM * kQTiles;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr int kMmaWarp = 8;
 constexpr int kLoadWarp = 9;
+constexpr uint32_t kRegsLaunch = 168;    // ptxas's allocation at 384 threads, 1 CTA/SM
+constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsOther = 72;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch,
+              "the warpgroup register split must fit in the registers the CTA launches with");
+// Lazy correction: a row keeps its exponent base until its max grows by more than
+// 2^8 (in the exp2 domain); p <= 256 meanwhile, exact after the final 1/l.
+constexpr float kRescaleThreshold = 8.0f;
+// Every kExpEmuEvery-th pair of exponentials in a 32-column chunk is computed with the
+// FMA-pipe polynomial (exp2_poly2) instead of MUFU ex2, balancing the two pipes (0 = none).
+#ifndef FA_EXP_EMU_EVERY
+#define FA_EXP_EMU_EVERY 0
+#endif
+constexpr int kExpEmuEvery = FA_EXP_EMU_EVERY;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
 
@@ -75,13 +92,16 @@ struct Cfg {
     static constexpr int kQOff = 0;
     static constexpr int kRingOff = kQTiles * kTileBytes;
     static constexpr int kBarOff = kRingOff + kStages * kTileBytes;
-    // q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2] o_full[2] epi[2] drain never
+    // q_full[2] kv_full[S] kv_empty[S] s_full[2] p_half[2] p_full[2] pv_half_done[2] o_full[2]
+    // epi[2] drain never
     static constexpr int kBarQFull = 0;
     static constexpr int kBarKvFull = 2;
     static constexpr int kBarKvEmpty = 2 + kStages;
     static constexpr int kBarSFull = 2 + 2 * kStages;
-    static constexpr int kBarPFull = kBarSFull + 2;
-    static constexpr int kBarOFull = kBarPFull + 2;
+    static constexpr int kBarPHalf = kBarSFull + 2;       // first 64 keys of P written
+    static constexpr int kBarPFull = kBarPHalf + 2;       // all of P written (and O corrected)
+    static constexpr int kBarPvHalf = kBarPFull + 2;      // first-half PV MMAs completed
+    static constexpr int kBarOFull = kBarPvHalf + 2;
     static constexpr int kBarEpi = kBarOFull + 2;
     static constexpr int kBarDrain = kBarEpi + 2;
     static constexpr int kBarNever = kBarDrain + 1;
@@ -169,14 +189,15 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_saddr, uint
     }
 }
 
-// O (+)= P V: 8 MMAs of M=128, N=D, K=16 keys. P comes from TMEM (16 keys =
+// O (+)= P V over key steps [kFirst, kLast) of 16 keys (8 in a tile): MMAs of
+// M=128, N=D, K=16. P comes from TMEM (16 keys =
 // 8 columns of packed bf16 pairs); V is MN-major: 64-column blocks kSubBytes
 // apart (LBO), 8-key row groups 1024 bytes apart (SBO).
-template <int D>
+template <int D, int kFirst, int kLast>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_saddr, bool accumulate)
 {
 #pragma unroll
-    for (int kk = 0; kk < kBlockN / 16; ++kk) {
+    for (int kk = kFirst; kk < kLast; ++kk) {
         const uint64_t b = make_smem_desc(v_saddr + static_cast<uint32_t>(kk * 16 * 128), kSubBytes, 1024);
         umma_ts(d_tmem, p_tmem + static_cast<uint32_t>(kk * 8), b, Cfg<D>::kIdescPV,
                 (accumulate || kk > 0) ? 1u : 0u);
@@ -227,7 +248,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         for (int t = 0; t < 2; ++t) {
             mbar_init(bar(C::kBarSFull + t), 1);
+            mbar_init(bar(C::kBarPHalf + t), kBlockM);
             mbar_init(bar(C::kBarPFull + t), kBlockM);
+            mbar_init(bar(C::kBarPvHalf + t), 1);
             mbar_init(bar(C::kBarOFull + t), 1);
             mbar_init(bar(C::kBarEpi + t), kBlockM);
         }
@@ -248,6 +271,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
     if (warp == kLoadWarp) {
         // ======================= TMA producer ==================================
+        regs_decrease<kRegsOther>();
         if (lane == 0) {
             tma_prefetch_map(&tm_q);
             tma_prefetch_map(&tm_k);
@@ -290,6 +314,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         __syncwarp();
     } else if (warp == kMmaWarp) {
         // ======================= MMA issuer ====================================
+        regs_decrease<kRegsOther>();
         if (lane == 0) {
             const uint32_t t_s0 = tmem_base + C::kColS0;
             const uint32_t t_s1 = tmem_base + C::kColS1;
@@ -319,10 +344,16 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 const int ki = 2 * j + 2;      // ring index of K_{j+1}
                 const bool more = j + 1 < n_kv;
                 const bool last = !more;
+                const uint32_t par = static_cast<uint32_t>(j & 1);
                 if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
-                if (!wait_bounded(bar(C::kBarPFull + 0), j & 1, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                // Tile 0: PV over the first 64 keys as soon as that half of P is in TMEM.
+                if (!wait_bounded(bar(C::kBarPHalf + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
                 tc_fence_after();
-                issue_pv<D>(t_o0, t_s0, slot_addr(vi), j > 0);
+                issue_pv<D, 0, 4>(t_o0, t_s0, slot_addr(vi), j > 0);
+                umma_commit(bar(C::kBarPvHalf + 0));
+                if (!wait_bounded(bar(C::kBarPFull + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv<D, 4, 8>(t_o0, t_s0, slot_addr(vi), true);
                 if (last) umma_commit(bar(C::kBarOFull + 0));
                 if (more) {
                     if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
@@ -330,9 +361,14 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     issue_qk<D>(t_s0, sq0, slot_addr(ki));
                     umma_commit(bar(C::kBarSFull + 0));
                 }
-                if (!wait_bounded(bar(C::kBarPFull + 1), j & 1, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
+                // Tile 1, same pattern.
+                if (!wait_bounded(bar(C::kBarPHalf + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
                 tc_fence_after();
-                issue_pv<D>(t_o1, t_s1, slot_addr(vi), j > 0);
+                issue_pv<D, 0, 4>(t_o1, t_s1, slot_addr(vi), j > 0);
+                umma_commit(bar(C::kBarPvHalf + 1));
+                if (!wait_bounded(bar(C::kBarPFull + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv<D, 4, 8>(t_o1, t_s1, slot_addr(vi), true);
                 umma_commit(empty_bar(vi));
                 if (last) umma_commit(bar(C::kBarOFull + 1));
                 if (more) {
@@ -346,8 +382,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             wait_drain(bar(C::kBarDrain), 0, timeout);
         }
         __syncwarp();
-    } else {
+    } else if (warp < kMmaWarp) {
         // ======================= softmax / correction / epilogue ================
+        regs_increase<kRegsSoftmax>();
         const int t = warp / 4;                    // Q tile of this warpgroup
         const int quarter = warp % 4;              // TMEM lane quarter of this warp
         const int r = quarter * 32 + lane;         // row within the Q tile == TMEM lane
@@ -362,6 +399,69 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         float row_max = -INFINITY;   // running max of raw scores
         float row_sum = 0.0f;        // running sum of exp2((s - max) * sl2), fp32 before rounding
         bool ok = true;
+
+        float m_base = 0.0f;         // row_max * sl2, the exp2 offset in use (0 while row_max = -inf)
+        const uint64_t c2 = f2_pack(sl2, sl2);
+
+        // O *= scale (per row) in TMEM; warp-collective.
+        auto rescale_o = [&](float scale) {
+            const uint64_t a2 = f2_pack(scale, scale);
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
+                tmem_wait_ld();
+                reg_fence32(o);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float o0, o1;
+                    f2_unpack(fmul2(f2_pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), a2), o0, o1);
+                    o[2 * i] = __float_as_uint(o0);
+                    o[2 * i + 1] = __float_as_uint(o1);
+                }
+                tmem_st32(t_o + static_cast<uint32_t>(c * 32), o);
+            }
+        };
+
+        // Exponentiate 64 scores (two 32-column chunks) against base `mb`, pack P to bf16
+        // pairs and accumulate the fp32 sum; also return the raw max of the 64 scores. The
+        // max and the exponentials are independent instruction streams.
+        auto exp_half = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], float mb, bool emulate,
+                            uint32_t (&out)[32], float& half_sum, float& half_max) {
+            const uint64_t nb2 = f2_pack(-mb, -mb);
+            uint64_t sum_a = f2_pack(0.0f, 0.0f), sum_b = f2_pack(0.0f, 0.0f);
+            float ma = __uint_as_float(lo[0]), mb_ = __uint_as_float(hi[0]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t (&src)[32] = (i < 16) ? lo : hi;
+                const int k = (i & 15) * 2;
+                if (k > 0 || i >= 16) {
+                    if (i < 16) ma = max3f(ma, __uint_as_float(src[k]), __uint_as_float(src[k + 1]));
+                    else mb_ = max3f(mb_, __uint_as_float(src[k]), __uint_as_float(src[k + 1]));
+                } else {
+                    ma = fmaxf(ma, __uint_as_float(src[1]));
+                }
+                const uint64_t x = ffma2(f2_pack(__uint_as_float(src[k]), __uint_as_float(src[k + 1])), c2, nb2);
+                uint64_t pr;
+                if (kExpEmuEvery > 0 && emulate && (i % (kExpEmuEvery > 0 ? kExpEmuEvery : 1)) == kExpEmuEvery - 1) {
+                    pr = exp2_poly2(x);
+                } else {
+                    float x0, x1;
+                    f2_unpack(x, x0, x1);
+                    pr = f2_pack(ex2_approx(x0), ex2_approx(x1));
+                }
+                if (i & 1) sum_b = fadd2(sum_b, pr);
+                else sum_a = fadd2(sum_a, pr);
+                float p0, p1;
+                f2_unpack(pr, p0, p1);
+                out[i] = pack_bf16x2(p0, p1);
+            }
+            float sa0, sa1, sb0, sb1;
+            f2_unpack(sum_a, sa0, sa1);
+            f2_unpack(sum_b, sb0, sb1);
+            half_sum = (sa0 + sa1) + (sb0 + sb1);
+            half_max = fmaxf(ma, mb_);
+        };
 
         for (int j = 0; j < n_kv; ++j) {
             ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarSFull + t), j & 1, abort_flag, timeout, kSiteSoftS));
@@ -389,49 +489,67 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                         if (key0 + c * 32 + i > limit) s[c][i] = __float_as_uint(-INFINITY);
             }
 
-            float m0 = row_max, m1 = row_max, m2 = row_max, m3 = row_max;
+            if (j == 0) {
+                // First tile: the base is the tile's row max (no exponent to keep yet).
+                float mx[4];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                m0 = fmaxf(m0, __uint_as_float(s[0][i]));
-                m1 = fmaxf(m1, __uint_as_float(s[1][i]));
-                m2 = fmaxf(m2, __uint_as_float(s[2][i]));
-                m3 = fmaxf(m3, __uint_as_float(s[3][i]));
-            }
-            const float m_new = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-            const float m_base = (m_new == -INFINITY) ? 0.0f : m_new * sl2;
-            const float alpha = ex2_approx(row_max * sl2 - m_base);
-
-            float sum0 = 0.0f, sum1 = 0.0f;
+                for (int c = 0; c < 4; ++c) {
+                    float a = __uint_as_float(s[c][0]), b = __uint_as_float(s[c][1]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t packed[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i]), sl2, -m_base));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i + 1]), sl2, -m_base));
-                    sum0 += p0;
-                    sum1 += p1;
-                    packed[i] = pack_bf16x2(p0, p1);
+                    for (int i = 2; i < 32; i += 4) {
+                        a = max3f(a, __uint_as_float(s[c][i]), __uint_as_float(s[c][i + 1]));
+                        b = max3f(b, __uint_as_float(s[c][i + 2]), __uint_as_float(s[c][i + 3]));
+                    }
+                    mx[c] = fmaxf(a, b);
                 }
-                tmem_st16(t_s + static_cast<uint32_t>(c * 16), packed);
+                row_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+                m_base = (row_max == -INFINITY) ? 0.0f : row_max * sl2;
             }
-            row_sum = row_sum * alpha + (sum0 + sum1);
 
-            // O correction: only when some row of this warp raised its max, and
-            // never before the first PV has written O.
-            if (j > 0 && __any_sync(0xffffffffu, m_new > row_max)) {
+            float o_scale = 1.0f;    // O correction owed before the first PV of this tile reads O
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
-                    tmem_wait_ld();
-                    reg_fence32(o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(t_o + static_cast<uint32_t>(c * 32), o);
+            for (int h = 0; h < 2; ++h) {
+                uint32_t packed[32];
+                float hsum, hmax;
+                exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax);
+                // Optimistic: the exponentials used the current base. If any score of this half
+                // exceeds it by more than the threshold (rare after the first tile), move the
+                // base, correct what was accumulated on the old one, and redo this half.
+                const bool need = (hmax - row_max) * sl2 > kRescaleThreshold;
+                if (__any_sync(0xffffffffu, need)) {
+                    const float m_new = need ? hmax : row_max;
+                    const float alpha = need ? ex2_approx(row_max * sl2 - m_new * sl2) : 1.0f;
+                    row_sum *= alpha;
+                    row_max = m_new;
+                    m_base = (row_max == -INFINITY) ? 0.0f : row_max * sl2;
+                    if (h == 0) {
+                        o_scale *= alpha;
+                    } else {
+                        // The first-half PV of this tile may be running on the old base: let it
+                        // finish, then correct O (including its contribution) now.
+                        ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarPvHalf + t), j & 1, abort_flag,
+                                                                  timeout, kSiteSoftO));
+                        if (!ok) break;
+                        tc_fence_after();
+                        rescale_o(alpha);
+                    }
+                    exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax);
+                }
+                row_sum += hsum;
+                uint32_t (&p_lo)[16] = *reinterpret_cast<uint32_t (*)[16]>(&packed[0]);
+                uint32_t (&p_hi)[16] = *reinterpret_cast<uint32_t (*)[16]>(&packed[16]);
+                tmem_st16(t_s + static_cast<uint32_t>(32 * h), p_lo);
+                tmem_st16(t_s + static_cast<uint32_t>(32 * h + 16), p_hi);
+                if (h == 0) {
+                    // Keys 0-63 of P are final: correct O first (the PV is the next reader of O;
+                    // at j = 0 it overwrites O), then hand the first half to the MMA.
+                    if (j > 0 && __any_sync(0xffffffffu, o_scale != 1.0f)) rescale_o(o_scale);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(bar(C::kBarPHalf + t));
                 }
             }
-            row_max = m_new;
+            if (!ok) break;
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::kBarPFull + t));
@@ -480,6 +598,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
         }
         tc_fence_before();
+    } else {
+        regs_decrease<kRegsOther>();   // warps 10-11: idle members of the third warpgroup
     }
 
     __syncthreads();
@@ -539,7 +659,20 @@ int prepare_device(int device)
         if (err == cudaSuccess)
             err = cudaFuncSetAttribute(fa_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg<128>::kSmemBytes);
-        if (err != cudaSuccess) state.status = static_cast<int>(err);
+        if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
+        // The warpgroup register split (setmaxnreg) waits forever if the CTA launched with
+        // fewer registers than it hands out: refuse to launch such a build.
+        for (const void* func : {reinterpret_cast<const void*>(fa_fwd_kernel<64>),
+                                 reinterpret_cast<const void*>(fa_fwd_kernel<128>)}) {
+            cudaFuncAttributes attributes{};
+            err = cudaFuncGetAttributes(&attributes, func);
+            if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
+            if (static_cast<uint32_t>(attributes.numRegs) * kThreads <
+                2u * 128u * kRegsSoftmax + 128u * kRegsOther) {
+                state.status = FA_STATUS_BUILD_MISMATCH;
+                return;
+            }
+        }
     });
     return state.status;
 }
@@ -740,6 +873,7 @@ const char* fa_sm100_status_string(int status)
         case FA_STATUS_TENSOR_MAP: return "tensor map encoding failed";
         case FA_STATUS_DEVICE_TIMEOUT: return "device-side wait timed out";
         case FA_STATUS_HOST_ALLOC: return "staging allocation failed";
+        case FA_STATUS_BUILD_MISMATCH: return "kernel built with fewer registers than its warpgroup split needs";
         default: break;
     }
     if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));

@@ -205,6 +205,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16])
+{
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
 {
     asm volatile(
@@ -314,6 +332,86 @@ __device__ __forceinline__ float ex2_approx(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max of three floats in one instruction.
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed pairs of f32 in one 64-bit register pair (sm_100 FFMA2/FADD2/FMUL2).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
+{
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Warpgroup register reallocation (all four warps of the warpgroup execute it).
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegs));
+}
+
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegs));
+}
+
+// 2^x for a pair of floats on the FMA/ALU pipes instead of MUFU. Cody-Waite style
+// split x = n + f with n = rint(x) (the 1.5*2^23 rounding constant) and f in
+// [-0.5, 0.5]; 2^f ~ 1 + f*(c1 + f*(c2 + f*c3)), a minimax polynomial for the
+// relative error with the constant term pinned to 1 (fitted here by linear
+// programming: max relative error 1.01e-4, 2^0 exact); 2^n is added into the
+// exponent field. x is clamped to >= -127, where the result is already ~1e-38.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x)
+{
+    float x0, x1;
+    f2_unpack(x, x0, x1);
+    const uint64_t xc = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
+    const uint64_t t = fadd2(xc, f2_pack(12582912.0f, 12582912.0f));
+    const uint64_t r = fadd2(t, f2_pack(-12582912.0f, -12582912.0f));
+    const uint64_t f = ffma2(r, f2_pack(-1.0f, -1.0f), xc);
+    uint64_t q = ffma2(f, f2_pack(0.055008937f, 0.055008937f), f2_pack(0.24221095f, 0.24221095f));
+    q = ffma2(q, f, f2_pack(0.6932829f, 0.6932829f));
+    q = ffma2(q, f, f2_pack(1.0f, 1.0f));
+    float q0, q1, t0, t1;
+    f2_unpack(q, q0, q1);
+    f2_unpack(t, t0, t1);
+    q0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    q1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+    return f2_pack(q0, q1);
 }
 
 // Two floats -> packed bf16x2 (round to nearest even); `lo` in bits 0-15.

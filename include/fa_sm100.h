@@ -41,6 +41,7 @@ extern "C" {
 #define FA_STATUS_TENSOR_MAP         1006 /* cuTensorMapEncodeTiled rejected a tensor */
 #define FA_STATUS_DEVICE_TIMEOUT     1007 /* a device-side bounded wait ran out (see fa_sm100_device_status) */
 #define FA_STATUS_HOST_ALLOC         1008 /* pinned/device staging memory could not be obtained */
+#define FA_STATUS_BUILD_MISMATCH     1009 /* kernel registers at launch cannot cover its warpgroup split */
 
 /* Resource report; same fields and meaning as the reference's FusedTilingInfo
  * (include/flash_attention.h:60-72). */

@@ -99,7 +99,7 @@ def test_rejected_arguments_without_gpu(lib):
 
 
 def test_status_strings(lib):
-    for code in (0, 1001, 1002, 1003, 1004, 1005, 1006, 1007, 1008):
+    for code in (0, 1001, 1002, 1003, 1004, 1005, 1006, 1007, 1008, 1009):
         assert lib.fa_sm100_status_string(code)
     assert b"unknown" in lib.fa_sm100_status_string(123456)
 

@@ -231,10 +231,10 @@ def test_host_entry_matches_device_entry(oracle, cuda_device):
 
 def test_against_reference_v3_built_for_sm100(oracle, cuda_device):
     """The reference's own v3 kernel (kernels/v3/v3_tensorcore.cu) built for sm_100a, run on the
-    same inputs, as a second opinion. Ours must pass the gate on every shape. v3 is held to the
-    gate only on the shape its own accuracy suite validates, (1,2,256,D)
-    (bench_flash_attention.cu:514-530); elsewhere its error is reported, not asserted: built for
-    sm_100a it exceeds the gate at longer sequences (e.g. (2,8,2048,64) causal)."""
+    same inputs, as a second opinion. Ours must pass the gate on every shape. v3's error is
+    reported, not asserted: built for sm_100a it exceeds the gate and is not run-to-run
+    deterministic on B200 (two launches on the same inputs can differ), even at its own accuracy
+    shape (1,2,256,D) which it passes on the reference's sm_86 GPU."""
     import torch
     ref_lib = oracle.load_reference()
     if ref_lib is None:
@@ -247,19 +247,23 @@ def test_against_reference_v3_built_for_sm100(oracle, cuda_device):
         q, k, v = oracle.make_inputs(b, h, n, d)
         ref = oracle.attention(q, k, v, b, h, n, d, causal)
         mine = run_kernel(q, k, v, AttentionShape(b, h, n, d), causal, cuda_device)
-        dq, dk, dv = _to_dev(q, cuda_device), _to_dev(k, cuda_device), _to_dev(v, cuda_device)
-        do = _poisoned_like(dq)
-        torch.cuda.synchronize()
-        rc = ref_lib.ref_launch_tensorcore_v3(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(),
-                                              b, h, n, d, causal, None)
-        assert rc == 0
-        torch.cuda.synchronize()
-        theirs = oracle.compare(_to_host_bits(do), ref, d, TOL)
+        mine_again = run_kernel(q, k, v, AttentionShape(b, h, n, d), causal, cuda_device)
         a_mine = assert_parity(mine, ref, d, "sm100")
-        report.append(f"({b},{h},{n},{d}) causal={causal}: sm100 {a_mine['ulp']:.2f} ulp, "
-                      f"v3@sm_100a {theirs['ulp']:.2f} ulp")
-        if (b, h, n) == (1, 2, 256):
-            assert theirs["passed"], ("v3", theirs)
+        assert np.array_equal(mine, mine_again)
+        dq, dk, dv = _to_dev(q, cuda_device), _to_dev(k, cuda_device), _to_dev(v, cuda_device)
+        runs = []
+        for _ in range(2):
+            do = _poisoned_like(dq)
+            torch.cuda.synchronize()
+            rc = ref_lib.ref_launch_tensorcore_v3(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(),
+                                                  b, h, n, d, causal, None)
+            assert rc == 0
+            torch.cuda.synchronize()
+            runs.append(_to_host_bits(do))
+        theirs = oracle.compare(runs[0], ref, d, TOL)
+        report.append(f"({b},{h},{n},{d}) causal={causal}: sm100 {a_mine['ulp']:.2f} ulp (deterministic), "
+                      f"v3@sm_100a {theirs['ulp']:.2f} ulp, v3 run-to-run identical: "
+                      f"{bool(np.array_equal(runs[0], runs[1]))}")
     print("\n".join(report))
 
 
@@ -289,7 +293,7 @@ def test_query_reports_resources(cuda_device):
     from cuda_fused_attention_b200 import query_sm100
     for d in (64, 128):
         info = query_sm100(d)
-        assert info["supported"] == 1 and info["block_size"] == 320 and info["tile_kv"] == 128
+        assert info["supported"] == 1 and info["block_size"] == 384 and info["tile_kv"] == 128
         assert info["rows_per_block"] == 256 and info["max_blocks_per_sm"] == 1
         assert info["local_bytes_per_thread"] < 64
     assert query_sm100(96)["supported"] == 0

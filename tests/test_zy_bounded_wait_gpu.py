@@ -1,0 +1,41 @@
+"""Failure detection on the GPU without a fault: a wait that runs out.
+
+fa_sm100_fwd_inject_stall makes the MMA warp wait on an mbarrier that nothing
+arrives on, with a 20 ms limit. The kernel must give up, record the wait site
+in the device error word, drain its own copies, free its tensor memory and
+return; the host reads FA_STATUS_DEVICE_TIMEOUT, and the same context then runs
+a normal forward correctly (tensor memory was released, nothing is stuck).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_injected_stall_times_out_and_context_survives(oracle, cuda_device):
+    import torch
+    from cuda_fused_attention_b200 import STATUS_DEVICE_TIMEOUT, AttentionShape, device_status, \
+        launch_attention_sm100
+    from cuda_fused_attention_b200 import _lib
+    lib = _lib.load()
+    b, h, n, d = 1, 2, 256, 64
+    q, k, v = oracle.make_inputs(b, h, n, d)
+    dev = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda_device) for x in (q, k, v)]
+    o = torch.empty_like(dev[0])
+    assert device_status() == (0, 0)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    rc = lib.fa_sm100_fwd_inject_stall(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), o.data_ptr(),
+                                       b, h, n, d, 0, 20_000_000, stream)
+    assert rc == 0
+    status, word = device_status()
+    assert status == STATUS_DEVICE_TIMEOUT
+    assert word & 1 and (word >> 8) & 0xFF == 10      # site 10: the injected wait
+    assert device_status() == (0, 0)                   # read-and-clear
+    # The context is intact: a normal launch right after is correct.
+    ref = oracle.attention(q, k, v, b, h, n, d, 1)
+    o.view(torch.int16).fill_(-1)
+    launch_attention_sm100(dev[0], dev[1], dev[2], o, AttentionShape(b, h, n, d), True)
+    torch.cuda.synchronize()
+    acc = oracle.compare(o.view(torch.int16).cpu().numpy().view(np.uint16), ref, d)
+    assert acc["passed"], acc
+    assert device_status() == (0, 0)
