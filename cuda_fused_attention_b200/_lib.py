@@ -20,6 +20,7 @@ STATUS_TENSOR_MAP = 1006
 STATUS_DEVICE_TIMEOUT = 1007
 STATUS_HOST_ALLOC = 1008
 STATUS_BUILD_MISMATCH = 1009
+STATUS_STATIC_TOO_LARGE = 1010
 
 #: Every symbol include/fa_sm100.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p
@@ -39,6 +40,8 @@ SIGNATURES = {
     "fa_sm100_fwd_inject_stall": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, ctypes.c_ulonglong, _VP]),
     "fa_sm100_fwd_host": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I]),
     "fa_sm100_release_staging": (_I, []),
+    "fa_sm100_fwd_host_static": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP]),
+    "fa_sm100_static_staging_bytes": (ctypes.c_size_t, []),
 }
 
 

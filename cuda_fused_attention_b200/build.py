@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libfa_sm100.so")
-SOURCES = ["fa_sm100.cu", "fa_sm100_host.cu", "fa_sm100_api.cu"]
+SOURCES = ["fa_sm100.cu", "fa_sm100_host.cu", "fa_sm100_api.cu", "fa_sm100_static.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -874,6 +874,7 @@ const char* fa_sm100_status_string(int status)
         case FA_STATUS_DEVICE_TIMEOUT: return "device-side wait timed out";
         case FA_STATUS_HOST_ALLOC: return "staging allocation failed";
         case FA_STATUS_BUILD_MISMATCH: return "kernel built with fewer registers than its warpgroup split needs";
+        case FA_STATUS_STATIC_TOO_LARGE: return "slab larger than the fixed staging of fa_sm100_fwd_host_static";
         default: break;
     }
     if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));

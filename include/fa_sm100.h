@@ -42,6 +42,7 @@ extern "C" {
 #define FA_STATUS_DEVICE_TIMEOUT     1007 /* a device-side bounded wait ran out (see fa_sm100_device_status) */
 #define FA_STATUS_HOST_ALLOC         1008 /* pinned/device staging memory could not be obtained */
 #define FA_STATUS_BUILD_MISMATCH     1009 /* kernel registers at launch cannot cover its warpgroup split */
+#define FA_STATUS_STATIC_TOO_LARGE   1010 /* a slab exceeds the fixed staging of fa_sm100_fwd_host_static */
 
 /* Resource report; same fields and meaning as the reference's FusedTilingInfo
  * (include/flash_attention.h:60-72). */
@@ -124,6 +125,23 @@ FA_API int fa_sm100_fwd_host(const void* q_host, const void* k_host, const void*
 
 /* Frees the staging buffers of fa_sm100_fwd_host on the current device. */
 FA_API int fa_sm100_release_staging(void);
+
+/* Host-buffer forward pass that allocates nothing, for callers that cannot
+ * allocate device memory (no cudaMalloc/cudaFree, no stream or event creation,
+ * no allocating library routine). No counterpart in the reference. Same result
+ * as fa_sm100_fwd_host; Q/K/V/O are staged through one fixed 32 MiB file-scope
+ * __device__ array (fa_sm100_static_staging_bytes()) that every GPU loading the
+ * library holds until exit, one slab (seq_len*head_dim bf16) at most 8 MiB,
+ * else FA_STATUS_STATIC_TOO_LARGE. Runs on `stream` (NULL = legacy default)
+ * and synchronises it. The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress) with that device current: make it before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * race, so serialise them. */
+FA_API int fa_sm100_fwd_host_static(const void* q_host, const void* k_host, const void* v_host, void* o_host,
+                                    int batch, int heads, int seq_len, int head_dim, int causal, void* stream);
+
+/* Size in bytes of the fixed staging array used by fa_sm100_fwd_host_static. */
+FA_API size_t fa_sm100_static_staging_bytes(void);
 
 #ifdef __cplusplus
 }  /* extern "C" */
