@@ -1,0 +1,129 @@
+"""Per-config timing report on the GPU: this kernel vs the reference's v3 built for sm_100a.
+
+For every BASELINE.json config (and mask) this times both kernels with the
+reference harness's protocol (bench_flash_attention.cu:43-44, :265-299: 5
+warm-ups, then 30 individually event-timed launches, median) on the same
+device buffers, and prints ms, TFLOP/s (reference FLOP count) and % of the
+measured bf16 peak. The assertion is the BASELINE requirement that the new
+kernel beats the reference's tensor-core kernel on B200 at every config with a
+full grid (configs 2-5); config 1 (2 CTAs) is a latency/plumbing case.
+"""
+import json
+import os
+import statistics
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = [
+    ("1", (1, 2, 128, 64), (0,), 0),
+    ("2", (2, 8, 2048, 64), (0, 1), 0),
+    ("3", (4, 16, 4096, 128), (1,), 5),
+    ("4", (1, 32, 16384, 128), (1,), 0),
+    ("5", (16, 32, 8192, 128), (0, 1), 0),
+]
+
+
+def _peak():
+    path = os.path.join(os.path.dirname(os.path.dirname(__file__)), "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0
+
+
+def _time(launch, warmup=5, iters=30):
+    import torch
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    samples = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        b.synchronize()
+        samples.append(a.elapsed_time(b))
+    return statistics.median(samples)
+
+
+def _graph_time(launch, reps=20):
+    """GPU-only time per launch: `reps` launches captured in one CUDA graph, replayed."""
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            launch(s.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(g, stream=s, capture_error_mode="relaxed"):
+            for _ in range(reps):
+                launch(s.cuda_stream)
+    except RuntimeError:
+        torch.cuda.synchronize()
+        return None
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        g.replay()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / (5 * reps)
+    del g
+    return ms
+
+
+def test_per_config_report(oracle, cuda_device):
+    import torch
+    from cuda_fused_attention_b200 import AttentionShape, attention_flops
+    from cuda_fused_attention_b200 import _lib
+    lib = _lib.load()
+    ref_lib = oracle.load_reference()
+    peak = _peak()
+    rows = []
+    for name, (b, h, n, d), masks, family in CONFIGS:
+        shape = AttentionShape(b, h, n, d)
+        g = torch.Generator(device=cuda_device)
+        ts = []
+        for seed in (11, 22, 33):
+            g.manual_seed(seed)
+            ts.append(torch.randn(shape.numel, generator=g, device=cuda_device).to(torch.bfloat16))
+        q, k, v = ts
+        if family == 5:
+            q = (q.float() * 4).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        ptrs = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr())
+        for causal in masks:
+            flops = attention_flops(shape, causal)
+            # Both kernels are called the same way: straight through their C entry points.
+            mine = lambda st=None: lib.fa_sm100_fwd(*ptrs, b, h, n, d, causal, st)
+            ms = _time(mine)
+            gms = _graph_time(mine) or ms
+            line = {"config": name, "shape": (b, h, n, d), "causal": causal, "sm100_ms": ms, "sm100_graph_ms": gms,
+                    "sm100_tflops": flops / ms / 1e9, "sm100_graph_tflops": flops / gms / 1e9,
+                    "sm100_pct_peak": 100 * flops / gms / 1e9 / peak}
+            if ref_lib is not None:
+                theirs = lambda st=None: ref_lib.ref_launch_tensorcore_v3(*ptrs, b, h, n, d, causal, st)
+                ref_ms = _time(theirs)
+                ref_gms = _graph_time(theirs) or ref_ms
+                line.update({"v3_ms": ref_ms, "v3_graph_ms": ref_gms, "v3_tflops": flops / ref_gms / 1e9,
+                             "speedup": ref_ms / ms, "graph_speedup": ref_gms / gms})
+            rows.append(line)
+        del q, k, v, o, ts
+        torch.cuda.empty_cache()
+    print("\nconfig shape causal | sm100 launch ms, graph ms, graph TFLOP/s, %peak | "
+          "v3@sm_100a launch ms, graph ms, graph TFLOP/s | speedup launch, graph")
+    for r in rows:
+        extra = (f"| {r['v3_ms']:.4f} {r['v3_graph_ms']:.4f} {r['v3_tflops']:.1f} | {r['speedup']:.2f}x "
+                 f"{r['graph_speedup']:.2f}x" if "v3_ms" in r else "| -")
+        print(f"{r['config']} {r['shape']} {r['causal']} | {r['sm100_ms']:.4f} {r['sm100_graph_ms']:.4f} "
+              f"{r['sm100_graph_tflops']:.1f} {r['sm100_pct_peak']:.1f}% {extra}")
+    print("PERF_REPORT_JSON " + json.dumps(rows))
+    for r in rows:
+        if r["config"] != "1" and "graph_speedup" in r:
+            assert r["graph_speedup"] > 1.0, r
