@@ -72,6 +72,16 @@ def measured_peak():
         return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s"
 
 
+def measured_sustained_peak():
+    """cuBLAS bf16 run back to back under the 1000 W power cap (MEASURED_PEAKS.json), or None."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["bf16_tflops_sustained"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def profile_traffic():
     """Per-launch DRAM bytes of the kernel from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "fa_fwd_kernel_traffic.json")
@@ -120,7 +130,7 @@ class ClockSampler:
             self.reader.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, power = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
@@ -131,13 +141,18 @@ class ClockSampler:
                 mx = float(parts[1])
             except ValueError:
                 continue
+            try:
+                power.append(float(parts[2]))
+            except ValueError:
+                pass
             for name, flag in zip(names, parts[3:7]):
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w": statistics.median(power) if power else None,
+                "power_max_w": max(power) if power else None}
 
 
 # ----------------------------------------------------------------------------- CPU legs
@@ -311,6 +326,7 @@ def run_ours(args):
     ms_step, dense_ms_max, causal_ms_max = max_over_ranks([total_ms / args.steps, dense_ms, causal_ms])
     value = flops_step_total / (ms_step * 1e-3) / 1e12
     peak, peak_src = measured_peak()
+    sustained = measured_sustained_peak()
     # Dominant (only) kernel: fa_fwd_kernel<128>; per-launch algorithmic FLOPs / mean launch time.
     achieved = (flops_dense_local + flops_causal_local) / ((dense_ms + causal_ms) * 1e-3) / 1e12
     traffic = profile_traffic()
@@ -379,6 +395,10 @@ def run_ours(args):
         "causal_tflops": (flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12) if 1 in masks else None,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src,
+                     # The kernel runs the GPU into its 1000 W cap within the timed region (clock
+                     # and power samples in "clocks"); cuBLAS measured under the same cap:
+                     "sustained_peak": sustained,
+                     "frac_vs_sustained": None if sustained is None else achieved / sustained,
                      "kernel": "fa_sm100::fa_fwd_kernel<128>",
                      "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
                      "traffic_note": None if traffic is None else traffic.get("note")},

@@ -78,6 +78,14 @@ def _graph_time(launch, reps=20):
     return ms
 
 
+def _device_status(lib):
+    import ctypes
+    import torch
+    torch.cuda.synchronize()
+    word = ctypes.c_uint(0)
+    return lib.fa_sm100_device_status(ctypes.byref(word))
+
+
 def test_per_config_report(oracle, cuda_device):
     import torch
     from cuda_fused_attention_b200 import AttentionShape, attention_flops
@@ -102,8 +110,11 @@ def test_per_config_report(oracle, cuda_device):
             flops = attention_flops(shape, causal)
             # Both kernels are called the same way: straight through their C entry points.
             mine = lambda st=None: lib.fa_sm100_fwd(*ptrs, b, h, n, d, causal, st)
+            assert mine() == 0
             ms = _time(mine)
             gms = _graph_time(mine) or ms
+            # A launch that gave up on a wait (bounded one-second waits) must not pass as a timing.
+            assert _device_status(lib) == 0, (name, causal)
             line = {"config": name, "shape": (b, h, n, d), "causal": causal, "sm100_ms": ms, "sm100_graph_ms": gms,
                     "sm100_tflops": flops / ms / 1e9, "sm100_graph_tflops": flops / gms / 1e9,
                     "sm100_pct_peak": 100 * flops / gms / 1e9 / peak}
