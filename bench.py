@@ -225,7 +225,7 @@ def run_reference_arm(args):
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -407,12 +407,32 @@ def run_ours(args):
         "gpu_launches": len(masks) * args.steps * world,
         "clocks": clocks.summary(),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
+
+
+# The result line goes to the process's original stdout; everything else that writes to
+# file descriptor 1 while the bench runs (NCCL prints its version banner there, for one)
+# is sent to stderr, so stdout carries exactly one JSON line.
+_RESULT_OUT = None
+
+
+def emit(line):
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _keep_stdout_for_result():
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 
 
 def main():
     args = parse_args()
+    _keep_stdout_for_result()
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_ours(args)
