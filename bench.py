@@ -191,6 +191,28 @@ def cpu_reference_sample(threads, seq_len, head_dim, use_reference=True):
     return flops, seconds, kind
 
 
+def cpu_single_thread_configs():
+    """The reference's reference_attention on one host thread at BASELINE configs 1 and 2
+    (dense), whole problems: {name: {"ms": ..., "gflops": ...}}, or None without oracle/_ref."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import fa_oracle
+    ref = fa_oracle.load_reference()
+    if ref is None:
+        return None
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    out = {}
+    for name, (b, h, n, d) in (("config1", (1, 2, 128, 64)), ("config2", (2, 8, 2048, 64))):
+        q, k, v = fa_oracle.make_inputs(b, h, n, d)
+        o = np.empty(b * h * n * d, np.float64)
+        t0 = time.perf_counter()
+        ref.ref_reference_attention(P(q), P(k), P(v), P(o), b, h, n, d, 0)
+        sec = time.perf_counter() - t0
+        out[name] = {"ms": sec * 1e3, "gflops": fa_oracle.attention_flops(b, h, n, d, 0) / sec / 1e9,
+                     "shape": [b, h, n, d], "causal": 0, "threads": 1}
+    return out
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -222,7 +244,8 @@ def run_reference_arm(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) bf16 (reference generator, seeds 11/22/33)",
         "impl": "reference",
         "config": {"workload": "BASELINE config 5 (16,32,8192,128) dense+causal, CPU sample", **CONFIG},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample,
+                         "single_thread": cpu_single_thread_configs()},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -373,7 +396,8 @@ def run_ours(args):
         f, s, kind = cpu_reference_sample(threads, n, d)
         cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
                "sample": f"{threads} whole (8192 x 128) slabs, one per host thread, alternating dense/causal, "
-                         f"{s:.1f} s wall"}
+                         f"{s:.1f} s wall",
+               "single_thread": cpu_single_thread_configs()}
 
     if world > 1:
         dist.destroy_process_group()
