@@ -427,7 +427,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // pairs and accumulate the fp32 sum; also return the raw max of the 64 scores. The
         // max and the exponentials are independent instruction streams.
         auto exp_half = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], float mb, bool emulate,
-                            uint32_t (&out)[32], float& half_sum, float& half_max) {
+                            uint32_t (&out)[32], float& half_sum, float& half_max, uint32_t p_tmem) {
             const uint64_t nb2 = f2_pack(-mb, -mb);
             uint64_t sum_a = f2_pack(0.0f, 0.0f), sum_b = f2_pack(0.0f, 0.0f);
             float ma = __uint_as_float(lo[0]), mb_ = __uint_as_float(hi[0]);
@@ -455,6 +455,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 float p0, p1;
                 f2_unpack(pr, p0, p1);
                 out[i] = pack_bf16x2(p0, p1);
+                // Each 16 packed pairs go to TMEM as soon as they are complete, so that little
+                // store latency is left to wait for before P is handed to the MMA.
+                if (i == 15) tmem_st16(p_tmem, *reinterpret_cast<uint32_t (*)[16]>(&out[0]));
+                if (i == 31) tmem_st16(p_tmem + 16, *reinterpret_cast<uint32_t (*)[16]>(&out[16]));
             }
             float sa0, sa1, sb0, sb1;
             f2_unpack(sum_a, sa0, sa1);
@@ -511,7 +515,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             for (int h = 0; h < 2; ++h) {
                 uint32_t packed[32];
                 float hsum, hmax;
-                exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax);
+                exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax,
+                         t_s + static_cast<uint32_t>(32 * h));
                 // Optimistic: the exponentials used the current base. If any score of this half
                 // exceeds it by more than the threshold (rare after the first tile), move the
                 // base, correct what was accumulated on the old one, and redo this half.
@@ -533,13 +538,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                         tc_fence_after();
                         rescale_o(alpha);
                     }
-                    exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax);
+                    exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax,
+                         t_s + static_cast<uint32_t>(32 * h));
                 }
                 row_sum += hsum;
-                uint32_t (&p_lo)[16] = *reinterpret_cast<uint32_t (*)[16]>(&packed[0]);
-                uint32_t (&p_hi)[16] = *reinterpret_cast<uint32_t (*)[16]>(&packed[16]);
-                tmem_st16(t_s + static_cast<uint32_t>(32 * h), p_lo);
-                tmem_st16(t_s + static_cast<uint32_t>(32 * h + 16), p_hi);
+                // P of this half is in TMEM (stored by exp_half; a redo above stored it again).
                 if (h == 0) {
                     // Keys 0-63 of P are final: correct O first (the PV is the next reader of O;
                     // at j = 0 it overwrites O), then hand the first half to the MMA.
