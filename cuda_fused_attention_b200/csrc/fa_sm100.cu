@@ -64,9 +64,14 @@ constexpr uint32_t kRegsSoftmax = 216;
 constexpr uint32_t kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch,
               "the warpgroup register split must fit in the registers the CTA launches with");
-// Lazy correction: a row keeps its exponent base until its max grows by more than
-// 2^8 (in the exp2 domain); p <= 256 meanwhile, exact after the final 1/l.
-constexpr float kRescaleThreshold = 8.0f;
+// Lazy correction: a row keeps its exponent base until one of its scores exceeds it by
+// more than 16 in the exp2 domain, so p <= 2^16 meanwhile; the final 1/l makes that exact.
+// P is bf16 (relative precision independent of magnitude) and O and l accumulate in fp32,
+// where N * 2^16 * |v| stays far from overflow for every accepted N (<= 2^30). A warp
+// moves its base (O correction + redo of 64 exponentials) when any of its 32 rows needs
+// it; with a threshold of 8 instead, peaky rows (Q scaled by 4, config 3) made that
+// happen often enough to cost ~30 %.
+constexpr float kRescaleThreshold = 16.0f;
 // Every kExpEmuEvery-th pair of exponentials in a 32-column chunk is computed with the
 // FMA-pipe polynomial (exp2_poly2) instead of MUFU ex2, balancing the two pipes (0 = none).
 #ifndef FA_EXP_EMU_EVERY

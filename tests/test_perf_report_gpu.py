@@ -2,7 +2,7 @@
 
 For every BASELINE.json config (and mask) this times both kernels with the
 reference harness's protocol (bench_flash_attention.cu:43-44, :265-299: 5
-warm-ups, then 30 individually event-timed launches, median) on the same
+warm-ups, then 30 individually event-timed launches, median and IQR) on the same
 device buffers, and prints ms, TFLOP/s (reference FLOP count) and % of the
 measured bf16 peak. The assertion is the BASELINE requirement that the new
 kernel beats the reference's tensor-core kernel on B200 at every config with a
@@ -46,7 +46,13 @@ def _time(launch, warmup=5, iters=30):
         b.record()
         b.synchronize()
         samples.append(a.elapsed_time(b))
-    return statistics.median(samples)
+    return statistics.median(samples), _iqr(samples)
+
+
+def _iqr(samples):
+    """Interquartile range (p75 - p25) of the event-timed launches, as the reference harness reports."""
+    q = statistics.quantiles(samples, n=4)
+    return q[2] - q[0]
 
 
 def _graph_time(launch, reps=20):
@@ -111,28 +117,29 @@ def test_per_config_report(oracle, cuda_device):
             # Both kernels are called the same way: straight through their C entry points.
             mine = lambda st=None: lib.fa_sm100_fwd(*ptrs, b, h, n, d, causal, st)
             assert mine() == 0
-            ms = _time(mine)
+            ms, iqr = _time(mine)
             gms = _graph_time(mine) or ms
             # A launch that gave up on a wait (bounded one-second waits) must not pass as a timing.
             assert _device_status(lib) == 0, (name, causal)
-            line = {"config": name, "shape": (b, h, n, d), "causal": causal, "sm100_ms": ms, "sm100_graph_ms": gms,
+            line = {"config": name, "shape": (b, h, n, d), "causal": causal, "sm100_ms": ms, "sm100_iqr_ms": iqr,
+                    "sm100_graph_ms": gms,
                     "sm100_tflops": flops / ms / 1e9, "sm100_graph_tflops": flops / gms / 1e9,
                     "sm100_pct_peak": 100 * flops / gms / 1e9 / peak}
             if ref_lib is not None:
                 theirs = lambda st=None: ref_lib.ref_launch_tensorcore_v3(*ptrs, b, h, n, d, causal, st)
-                ref_ms = _time(theirs)
+                ref_ms, ref_iqr = _time(theirs)
                 ref_gms = _graph_time(theirs) or ref_ms
-                line.update({"v3_ms": ref_ms, "v3_graph_ms": ref_gms, "v3_tflops": flops / ref_gms / 1e9,
+                line.update({"v3_ms": ref_ms, "v3_iqr_ms": ref_iqr, "v3_graph_ms": ref_gms, "v3_tflops": flops / ref_gms / 1e9,
                              "speedup": ref_ms / ms, "graph_speedup": ref_gms / gms})
             rows.append(line)
         del q, k, v, o, ts
         torch.cuda.empty_cache()
-    print("\nconfig shape causal | sm100 launch ms, graph ms, graph TFLOP/s, %peak | "
-          "v3@sm_100a launch ms, graph ms, graph TFLOP/s | speedup launch, graph")
+    print("\nconfig shape causal | sm100 launch ms (IQR), graph ms, graph TFLOP/s, %peak | "
+          "v3@sm_100a launch ms (IQR), graph ms, graph TFLOP/s | speedup launch, graph")
     for r in rows:
-        extra = (f"| {r['v3_ms']:.4f} {r['v3_graph_ms']:.4f} {r['v3_tflops']:.1f} | {r['speedup']:.2f}x "
+        extra = (f"| {r['v3_ms']:.4f} ({r['v3_iqr_ms']:.4f}) {r['v3_graph_ms']:.4f} {r['v3_tflops']:.1f} | {r['speedup']:.2f}x "
                  f"{r['graph_speedup']:.2f}x" if "v3_ms" in r else "| -")
-        print(f"{r['config']} {r['shape']} {r['causal']} | {r['sm100_ms']:.4f} {r['sm100_graph_ms']:.4f} "
+        print(f"{r['config']} {r['shape']} {r['causal']} | {r['sm100_ms']:.4f} ({r['sm100_iqr_ms']:.4f}) {r['sm100_graph_ms']:.4f} "
               f"{r['sm100_graph_tflops']:.1f} {r['sm100_pct_peak']:.1f}% {extra}")
     print("PERF_REPORT_JSON " + json.dumps(rows))
     for r in rows:
