@@ -244,24 +244,15 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const int n_kv = p.causal ? min(kv_tiles_all, 2 * pair + 2) : kv_tiles_all;
 
     // ---- set-up ---------------------------------------------------------------
-    if (threadIdx.x == 0) {
-        mbar_init(bar(C::kBarQFull + 0), 1);
-        mbar_init(bar(C::kBarQFull + 1), 1);
-        for (int s = 0; s < C::kStages; ++s) {
-            mbar_init(bar(C::kBarKvFull + s), 1);
-            mbar_init(bar(C::kBarKvEmpty + s), 1);
+    // Barrier set-up, one barrier per lane of warp 0: p_half, p_full and epi count the 128
+    // threads of a softmax warpgroup, every other barrier a single arrival (an expect_tx, a
+    // tcgen05.commit or the inject-stall barrier nobody arrives on).
+    if (warp == 0) {
+        for (int b = lane; b < C::kNumBars; b += 32) {
+            const bool per_thread = (b >= C::kBarPHalf && b < C::kBarPvHalf) || (b >= C::kBarEpi && b < C::kBarDrain);
+            mbar_init(bar(b), per_thread ? kBlockM : 1);
         }
-        for (int t = 0; t < 2; ++t) {
-            mbar_init(bar(C::kBarSFull + t), 1);
-            mbar_init(bar(C::kBarPHalf + t), kBlockM);
-            mbar_init(bar(C::kBarPFull + t), kBlockM);
-            mbar_init(bar(C::kBarPvHalf + t), 1);
-            mbar_init(bar(C::kBarOFull + t), 1);
-            mbar_init(bar(C::kBarEpi + t), kBlockM);
-        }
-        mbar_init(bar(C::kBarDrain), 1);
-        mbar_init(bar(C::kBarNever), 1);
-        *abort_flag = 0u;
+        if (lane == 0) *abort_flag = 0u;
         fence_mbarrier_init();
     }
     if (warp == kMmaWarp) {
