@@ -41,6 +41,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -132,6 +133,8 @@ struct Params {
     int causal;
     int inject_stall;           // test only: the MMA warp waits on a barrier nothing arrives on
     unsigned long long timeout_ns;
+    long long num_slabs;        // slabs in this launch
+    int chunk;                  // causal block order: slabs per group (see the kernel's work item)
 };
 
 // Device error word of this module instance (one per device). Bit 0: some wait
@@ -232,11 +235,28 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
 
-    // ---- work item: slab-major, heaviest causal tiles of a slab first --------
+    // ---- work item ---------------------------------------------------------------
+    // Dense: slab-major (the CTAs of a slab run together and share its K/V through L2).
+    // Causal: slabs in groups of p.chunk; within a group the row pairs go heaviest first,
+    // each pair for every slab of the group, so the longest CTAs of the last slabs do not
+    // start late and stretch the tail, while the K/V of only one group (sized on the host
+    // to a fraction of L2) is being read at a time.
     const long long block = blockIdx.x;
-    const long long slab_local = block / p.num_pairs;
-    int pair = static_cast<int>(block - slab_local * p.num_pairs);
-    if (p.causal) pair = p.num_pairs - 1 - pair;
+    long long slab_local;
+    int pair;
+    if (p.causal) {
+        const long long per_group = static_cast<long long>(p.chunk) * p.num_pairs;
+        const long long group = block / per_group;
+        const long long first = group * p.chunk;
+        const long long in_group = min(static_cast<long long>(p.chunk), p.num_slabs - first);
+        const long long within = block - group * per_group;
+        const long long level = within / in_group;
+        slab_local = first + (within - level * in_group);
+        pair = p.num_pairs - 1 - static_cast<int>(level);
+    } else {
+        slab_local = block / p.num_pairs;
+        pair = static_cast<int>(block - slab_local * p.num_pairs);
+    }
     const int slab = static_cast<int>(p.slab_begin + slab_local);
     const int q_row0 = pair * kRowsPerCta;
     const int n = p.seq_len;
@@ -752,6 +772,13 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     params.timeout_ns = timeout_ns;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const long long count = slab_end - slab_begin;
+    params.num_slabs = count;
+    {
+        // Causal groups: as many slabs as keep the group's K and V within 32 MB of L2.
+        const long long kv_bytes = 4LL * seq_len * head_dim;
+        const long long by_l2 = kv_bytes > 0 ? (32LL << 20) / kv_bytes : count;
+        params.chunk = static_cast<int>(std::max(1LL, std::min(count, by_l2)));
+    }
     return head_dim == 64 ? launch<64>(mq, mk, mv, mo, params, count, s)
                           : launch<128>(mq, mk, mv, mo, params, count, s);
 }
