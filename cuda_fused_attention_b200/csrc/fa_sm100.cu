@@ -17,9 +17,11 @@
 //     swizzle, zero fill past N) into a K/V ring of mbarrier-guarded stages.
 //   * Softmax is one thread per row: a thread loads its whole S row from TMEM,
 //     so the row max and row sum need no shuffles. exp is ex2 with log2(e)
-//     folded into the scale. O is rescaled in TMEM only when a row max grows.
+//     folded into the scale. A row's exponent base moves (and O is rescaled in
+//     TMEM) only when one of its scores exceeds the base by a factor 2^16.
 //   * Causal: key tiles above the diagonal are never loaded or computed; only
-//     the diagonal tile(s) and a ragged tail tile take the element mask.
+//     the diagonal tile(s) and a ragged tail tile take the element mask. Blocks
+//     run in groups of slabs sized to L2, heaviest row pairs first across a group.
 //   * Epilogue: O from TMEM, times 1/l, to bf16, into the (now free) Q tile of
 //     shared memory in the swizzled layout, then one TMA store per 64 columns.
 //
