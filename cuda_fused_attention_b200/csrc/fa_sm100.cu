@@ -75,12 +75,6 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunc
 // it; with a threshold of 8 instead, peaky rows (Q scaled by 4, config 3) made that
 // happen often enough to cost ~30 %.
 constexpr float kRescaleThreshold = 16.0f;
-// Every kExpEmuEvery-th pair of exponentials in a 32-column chunk is computed with the
-// FMA-pipe polynomial (exp2_poly2) instead of MUFU ex2, balancing the two pipes (0 = none).
-#ifndef FA_EXP_EMU_EVERY
-#define FA_EXP_EMU_EVERY 0
-#endif
-constexpr int kExpEmuEvery = FA_EXP_EMU_EVERY;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
 
@@ -444,7 +438,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // Exponentiate 64 scores (two 32-column chunks) against base `mb`, pack P to bf16
         // pairs and accumulate the fp32 sum; also return the raw max of the 64 scores. The
         // max and the exponentials are independent instruction streams.
-        auto exp_half = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], float mb, bool emulate,
+        auto exp_half = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], float mb,
                             uint32_t (&out)[32], float& half_sum, float& half_max, uint32_t p_tmem) {
             const uint64_t nb2 = f2_pack(-mb, -mb);
             uint64_t sum_a = f2_pack(0.0f, 0.0f), sum_b = f2_pack(0.0f, 0.0f);
@@ -460,14 +454,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     ma = fmaxf(ma, __uint_as_float(src[1]));
                 }
                 const uint64_t x = ffma2(f2_pack(__uint_as_float(src[k]), __uint_as_float(src[k + 1])), c2, nb2);
-                uint64_t pr;
-                if (kExpEmuEvery > 0 && emulate && (i % (kExpEmuEvery > 0 ? kExpEmuEvery : 1)) == kExpEmuEvery - 1) {
-                    pr = exp2_poly2(x);
-                } else {
-                    float x0, x1;
-                    f2_unpack(x, x0, x1);
-                    pr = f2_pack(ex2_approx(x0), ex2_approx(x1));
-                }
+                float x0, x1;
+                f2_unpack(x, x0, x1);
+                const uint64_t pr = f2_pack(ex2_approx(x0), ex2_approx(x1));
                 if (i & 1) sum_b = fadd2(sum_b, pr);
                 else sum_a = fadd2(sum_a, pr);
                 float p0, p1;
@@ -533,7 +522,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             for (int h = 0; h < 2; ++h) {
                 uint32_t packed[32];
                 float hsum, hmax;
-                exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax,
+                exp_half(s[2 * h], s[2 * h + 1], m_base, packed, hsum, hmax,
                          t_s + static_cast<uint32_t>(32 * h));
                 // Optimistic: the exponentials used the current base. If any score of this half
                 // exceeds it by more than the threshold (rare after the first tile), move the
@@ -556,7 +545,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                         tc_fence_after();
                         rescale_o(alpha);
                     }
-                    exp_half(s[2 * h], s[2 * h + 1], m_base, !mask_tile, packed, hsum, hmax,
+                    exp_half(s[2 * h], s[2 * h + 1], m_base, packed, hsum, hmax,
                          t_s + static_cast<uint32_t>(32 * h));
                 }
                 row_sum += hsum;

@@ -389,31 +389,6 @@ __device__ __forceinline__ void regs_decrease()
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegs));
 }
 
-// 2^x for a pair of floats on the FMA/ALU pipes instead of MUFU. Cody-Waite style
-// split x = n + f with n = rint(x) (the 1.5*2^23 rounding constant) and f in
-// [-0.5, 0.5]; 2^f ~ 1 + f*(c1 + f*(c2 + f*c3)), a minimax polynomial for the
-// relative error with the constant term pinned to 1 (fitted here by linear
-// programming: max relative error 1.01e-4, 2^0 exact); 2^n is added into the
-// exponent field. x is clamped to >= -127, where the result is already ~1e-38.
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x)
-{
-    float x0, x1;
-    f2_unpack(x, x0, x1);
-    const uint64_t xc = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
-    const uint64_t t = fadd2(xc, f2_pack(12582912.0f, 12582912.0f));
-    const uint64_t r = fadd2(t, f2_pack(-12582912.0f, -12582912.0f));
-    const uint64_t f = ffma2(r, f2_pack(-1.0f, -1.0f), xc);
-    uint64_t q = ffma2(f, f2_pack(0.055008937f, 0.055008937f), f2_pack(0.24221095f, 0.24221095f));
-    q = ffma2(q, f, f2_pack(0.6932829f, 0.6932829f));
-    q = ffma2(q, f, f2_pack(1.0f, 1.0f));
-    float q0, q1, t0, t1;
-    f2_unpack(q, q0, q1);
-    f2_unpack(t, t0, t1);
-    q0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-    q1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-    return f2_pack(q0, q1);
-}
-
 // Two floats -> packed bf16x2 (round to nearest even); `lo` in bits 0-15.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
 {
