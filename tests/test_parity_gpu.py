@@ -194,6 +194,37 @@ def test_deterministic_and_stream(oracle, cuda_device):
     assert np.array_equal(first, second)
 
 
+def test_cached_tensor_maps_follow_pointers_and_shape(oracle, cuda_device):
+    """The launcher reuses encoded tensor maps per (pointers, shape). Six buffer sets (more than
+    the per-thread cache holds), launched twice in turn, and one set of allocations launched
+    as three different shapes and then the first again, must each match the oracle."""
+    import torch
+    from cuda_fused_attention_b200 import AttentionShape, launch_attention_sm100
+    count = 2 * 200 * 64
+    sets = []
+    for i in range(6):
+        q, k, v = (oracle.fill_normal(count, 100 + 3 * i + j) for j in range(3))
+        dq, dk, dv = (_to_dev(x, cuda_device) for x in (q, k, v))
+        sets.append(((q, k, v), (dq, dk, dv, _poisoned_like(dq))))
+
+    def launch_and_check(host, dev, b, h, n, d, causal):
+        q, k, v = host
+        dq, dk, dv, do = dev
+        do.view(torch.int16).fill_(-1)
+        launch_attention_sm100(dq, dk, dv, do, AttentionShape(b, h, n, d), causal)
+        torch.cuda.synchronize()
+        ref = oracle.attention(q, k, v, b, h, n, d, causal)
+        assert_parity(_to_host_bits(do), ref, d, ("cached maps", b, h, n, d, causal))
+
+    for _ in range(2):
+        for host, dev in sets:
+            launch_and_check(host, dev, 1, 2, 200, 64, 1)
+    host, dev = sets[0]
+    for b, h, n, d in [(1, 4, 100, 64), (1, 1, 200, 128), (2, 2, 50, 128), (1, 2, 200, 64)]:
+        launch_and_check(host, dev, b, h, n, d, 0)
+    check_device_clean()
+
+
 def test_slab_range_writes_only_its_slabs(oracle, cuda_device):
     import torch
     from cuda_fused_attention_b200 import AttentionShape, launch_attention_sm100_slabs
