@@ -7,7 +7,9 @@
 // registers, cp.async double buffering and warp-level mma.sync. Here:
 //
 //   * One CTA owns 256 query rows of one (batch, head) slab, as two 128-row Q
-//     tiles that ping-pong between two softmax warpgroups.
+//     tiles that ping-pong between two softmax warpgroups. When a grid of such
+//     CTAs would fill less than half the GPU, each CTA takes a single Q tile
+//     (the second warpgroup idles), doubling the CTAs and shortening the path.
 //   * QK^T and PV are tcgen05.mma (kind::f16, M=128, N=128 / N=D, BF16 in,
 //     FP32 accumulate) issued by one thread of the MMA warp. S and O live in
 //     tensor memory: S0 | S1 | O0 | O1 = 512 columns at D=128.
@@ -57,7 +59,7 @@ namespace fa_sm100 {
 
 constexpr int kBlockM = 128;    // query rows per Q tile == TMEM lanes
 constexpr int kBlockN = 128;    // keys per K/V tile
-constexpr int kQTiles = 2;      // Q tiles per CTA
+constexpr int kQTiles = 2;      // Q tiles per CTA (a row pair); small grids use one
 constexpr int kRowsPerCta = kBlockM * kQTiles;
 constexpr int kThreads = 384;
 constexpr int kMmaWarp = 8;
@@ -123,7 +125,7 @@ struct Cfg {
 
 struct Params {
     int seq_len;
-    int num_pairs;              // ceil(seq_len / 256): CTAs per slab
+    int num_units;              // CTAs per slab: ceil(seq_len / 256), or / 128 for the one-tile kernel
     long long slab_begin;       // first slab of this launch in the full tensor
     float scale_log2;           // default_scale(D) * log2(e)
     int causal;
@@ -208,7 +210,10 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
     }
 }
 
-template <int D>
+// kOneTile = false: a CTA per row pair (two Q tiles). kOneTile = true: a CTA per 128-row
+// Q tile, for grids too small to fill the GPU with pairs; warpgroup 1 then idles. Two
+// instantiations, so that the pair kernel carries no branch for the single-tile case.
+template <int D, bool kOneTile>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -232,32 +237,36 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const int lane = threadIdx.x % 32;
 
     // ---- work item ---------------------------------------------------------------
+    // A unit is p.tile_span consecutive 128-row Q tiles of one slab: a row pair (256 rows),
+    // or one tile when the host found the grid of pairs too small to fill the GPU.
     // Dense: slab-major (the CTAs of a slab run together and share its K/V through L2).
-    // Causal: slabs in groups of p.chunk; within a group the row pairs go heaviest first,
-    // each pair for every slab of the group, so the longest CTAs of the last slabs do not
+    // Causal: slabs in groups of p.chunk; within a group the units go heaviest first,
+    // each unit for every slab of the group, so the longest CTAs of the last slabs do not
     // start late and stretch the tail, while the K/V of only one group (sized on the host
     // to a fraction of L2) is being read at a time.
     const long long block = blockIdx.x;
     long long slab_local;
-    int pair;
+    int unit;
     if (p.causal) {
-        const long long per_group = static_cast<long long>(p.chunk) * p.num_pairs;
+        const long long per_group = static_cast<long long>(p.chunk) * p.num_units;
         const long long group = block / per_group;
         const long long first = group * p.chunk;
         const long long in_group = min(static_cast<long long>(p.chunk), p.num_slabs - first);
         const long long within = block - group * per_group;
         const long long level = within / in_group;
         slab_local = first + (within - level * in_group);
-        pair = p.num_pairs - 1 - static_cast<int>(level);
+        unit = p.num_units - 1 - static_cast<int>(level);
     } else {
-        slab_local = block / p.num_pairs;
-        pair = static_cast<int>(block - slab_local * p.num_pairs);
+        slab_local = block / p.num_units;
+        unit = static_cast<int>(block - slab_local * p.num_units);
     }
     const int slab = static_cast<int>(p.slab_begin + slab_local);
-    const int q_row0 = pair * kRowsPerCta;
+    constexpr bool two = !kOneTile;                      // a second Q tile in this CTA
+    const int tile0 = unit * (two ? kQTiles : 1);        // first 128-row Q tile of this CTA
+    const int q_row0 = tile0 * kBlockM;
     const int n = p.seq_len;
     const int kv_tiles_all = (n + kBlockN - 1) / kBlockN;
-    const int n_kv = p.causal ? min(kv_tiles_all, 2 * pair + 2) : kv_tiles_all;
+    const int n_kv = p.causal ? min(kv_tiles_all, tile0 + (two ? 2 : 1)) : kv_tiles_all;
 
     // ---- set-up ---------------------------------------------------------------
     // Barrier set-up, one barrier per lane of warp 0: p_half, p_full and epi count the 128
@@ -289,7 +298,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             tma_prefetch_map(&tm_k);
             tma_prefetch_map(&tm_v);
             tma_prefetch_map(&tm_o);
-            for (int t = 0; t < 2; ++t) {
+            for (int t = 0; t < (two ? 2 : 1); ++t) {
                 mbar_arrive_expect_tx(bar(C::kBarQFull + t), C::kTileBytes);
 #pragma unroll
                 for (int s = 0; s < C::kSub; ++s)
@@ -318,7 +327,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             if (!ok) {
                 // Abort: let every copy this CTA started land before shared memory goes away.
                 wait_drain(bar(C::kBarQFull + 0), 0, timeout);
-                wait_drain(bar(C::kBarQFull + 1), 0, timeout);
+                if (two) wait_drain(bar(C::kBarQFull + 1), 0, timeout);
                 for (int i = max(0, issued - C::kStages); i < issued; ++i)
                     wait_drain(bar(C::kBarKvFull + i % C::kStages), (i / C::kStages) & 1, timeout);
             }
@@ -340,53 +349,86 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             auto full_par = [&](int i) -> uint32_t { return static_cast<uint32_t>((i / C::kStages) & 1); };
 
             bool ok = wait_bounded(bar(C::kBarQFull + 0), 0, abort_flag, timeout, kSiteMmaQ) &&
-                      wait_bounded(bar(C::kBarQFull + 1), 0, abort_flag, timeout, kSiteMmaQ);
+                      (!two || wait_bounded(bar(C::kBarQFull + 1), 0, abort_flag, timeout, kSiteMmaQ));
             if (ok && p.inject_stall) ok = wait_bounded(bar(C::kBarNever), 0, abort_flag, timeout, kSiteInjected);
             if (ok) ok = wait_bounded(full_bar(0), full_par(0), abort_flag, timeout, kSiteMmaK);
-            if (ok) {
-                tc_fence_after();
-                issue_qk<D>(t_s0, sq0, slot_addr(0));
-                umma_commit(bar(C::kBarSFull + 0));
-                issue_qk<D>(t_s1, sq1, slot_addr(0));
-                umma_commit(bar(C::kBarSFull + 1));
-                umma_commit(empty_bar(0));
-            }
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const int vi = 2 * j + 1;      // ring index of V_j
-                const int ki = 2 * j + 2;      // ring index of K_{j+1}
-                const bool more = j + 1 < n_kv;
-                const bool last = !more;
-                const uint32_t par = static_cast<uint32_t>(j & 1);
-                if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
-                // Tile 0: PV over the first 64 keys as soon as that half of P is in TMEM.
-                if (!wait_bounded(bar(C::kBarPHalf + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv<D, 0, 4>(t_o0, t_s0, slot_addr(vi), j > 0);
-                umma_commit(bar(C::kBarPvHalf + 0));
-                if (!wait_bounded(bar(C::kBarPFull + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv<D, 4, 8>(t_o0, t_s0, slot_addr(vi), true);
-                if (last) umma_commit(bar(C::kBarOFull + 0));
-                if (more) {
-                    if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
+            if constexpr (two) {
+                if (ok) {
                     tc_fence_after();
-                    issue_qk<D>(t_s0, sq0, slot_addr(ki));
+                    issue_qk<D>(t_s0, sq0, slot_addr(0));
                     umma_commit(bar(C::kBarSFull + 0));
-                }
-                // Tile 1, same pattern.
-                if (!wait_bounded(bar(C::kBarPHalf + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv<D, 0, 4>(t_o1, t_s1, slot_addr(vi), j > 0);
-                umma_commit(bar(C::kBarPvHalf + 1));
-                if (!wait_bounded(bar(C::kBarPFull + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv<D, 4, 8>(t_o1, t_s1, slot_addr(vi), true);
-                umma_commit(empty_bar(vi));
-                if (last) umma_commit(bar(C::kBarOFull + 1));
-                if (more) {
-                    issue_qk<D>(t_s1, sq1, slot_addr(ki));
+                    issue_qk<D>(t_s1, sq1, slot_addr(0));
                     umma_commit(bar(C::kBarSFull + 1));
-                    umma_commit(empty_bar(ki));
+                    umma_commit(empty_bar(0));
+                }
+                for (int j = 0; ok && j < n_kv; ++j) {
+                    const int vi = 2 * j + 1;      // ring index of V_j
+                    const int ki = 2 * j + 2;      // ring index of K_{j+1}
+                    const bool more = j + 1 < n_kv;
+                    const bool last = !more;
+                    const uint32_t par = static_cast<uint32_t>(j & 1);
+                    if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
+                    // Tile 0: PV over the first 64 keys as soon as that half of P is in TMEM.
+                    if (!wait_bounded(bar(C::kBarPHalf + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 0, 4>(t_o0, t_s0, slot_addr(vi), j > 0);
+                    umma_commit(bar(C::kBarPvHalf + 0));
+                    if (!wait_bounded(bar(C::kBarPFull + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 4, 8>(t_o0, t_s0, slot_addr(vi), true);
+                    if (last) umma_commit(bar(C::kBarOFull + 0));
+                    if (more) {
+                        if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
+                        tc_fence_after();
+                        issue_qk<D>(t_s0, sq0, slot_addr(ki));
+                        umma_commit(bar(C::kBarSFull + 0));
+                    }
+                    // Tile 1, same pattern.
+                    if (!wait_bounded(bar(C::kBarPHalf + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 0, 4>(t_o1, t_s1, slot_addr(vi), j > 0);
+                    umma_commit(bar(C::kBarPvHalf + 1));
+                    if (!wait_bounded(bar(C::kBarPFull + 1), par, abort_flag, timeout, kSiteMmaP1)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 4, 8>(t_o1, t_s1, slot_addr(vi), true);
+                    umma_commit(empty_bar(vi));
+                    if (last) umma_commit(bar(C::kBarOFull + 1));
+                    if (more) {
+                        issue_qk<D>(t_s1, sq1, slot_addr(ki));
+                        umma_commit(bar(C::kBarSFull + 1));
+                        umma_commit(empty_bar(ki));
+                    }
+                }
+            } else {
+                // One Q tile (tile 0 only): the same pipeline without tile 1's MMAs.
+                if (ok) {
+                    tc_fence_after();
+                    issue_qk<D>(t_s0, sq0, slot_addr(0));
+                    umma_commit(bar(C::kBarSFull + 0));
+                    umma_commit(empty_bar(0));
+                }
+                for (int j = 0; ok && j < n_kv; ++j) {
+                    const int vi = 2 * j + 1;
+                    const int ki = 2 * j + 2;
+                    const bool more = j + 1 < n_kv;
+                    const uint32_t par = static_cast<uint32_t>(j & 1);
+                    if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
+                    if (!wait_bounded(bar(C::kBarPHalf + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 0, 4>(t_o0, t_s0, slot_addr(vi), j > 0);
+                    umma_commit(bar(C::kBarPvHalf + 0));
+                    if (!wait_bounded(bar(C::kBarPFull + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 4, 8>(t_o0, t_s0, slot_addr(vi), true);
+                    umma_commit(empty_bar(vi));
+                    if (!more) umma_commit(bar(C::kBarOFull + 0));
+                    if (more) {
+                        if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
+                        tc_fence_after();
+                        issue_qk<D>(t_s0, sq0, slot_addr(ki));
+                        umma_commit(bar(C::kBarSFull + 0));
+                        umma_commit(empty_bar(ki));
+                    }
                 }
             }
             // Every MMA issued above must finish before tensor memory is released.
@@ -394,7 +436,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             wait_drain(bar(C::kBarDrain), 0, timeout);
         }
         __syncwarp();
-    } else if (warp < kMmaWarp) {
+    } else if (warp < 4 || (warp < kMmaWarp && two)) {
         // ======================= softmax / correction / epilogue ================
         regs_increase<kRegsSoftmax>();
         const int t = warp / 4;                    // Q tile of this warpgroup
@@ -405,7 +447,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const uint32_t t_o = lane_base + (t == 0 ? C::kColO0 : C::kColO1);
         const int row = q_row0 + t * kBlockM + r;            // query index in the slab
         const int limit = p.causal ? min(row, n - 1) : n - 1;  // last key this row attends to
-        const int diag_tile = 2 * pair + t;                  // first key tile that needs the causal mask
+        const int diag_tile = tile0 + t;                     // first key tile that needs the causal mask
         const float sl2 = p.scale_log2;
 
         float row_max = -INFINITY;   // running max of raw scores
@@ -609,7 +651,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         tc_fence_before();
     } else {
-        regs_decrease<kRegsOther>();   // warps 10-11: idle members of the third warpgroup
+        // Warps 10-11 (idle members of the third warpgroup), and warpgroup 1 when the CTA has
+        // no second Q tile.
+        regs_decrease<kRegsOther>();
     }
 
     __syncthreads();
@@ -653,6 +697,7 @@ EncodeTiledFn encode_fn()
 struct DeviceState {
     std::once_flag once;
     int status = FA_STATUS_OK;
+    int sm_count = 0;
 };
 DeviceState g_devices[kMaxDevices];
 
@@ -665,15 +710,26 @@ int prepare_device(int device)
         cudaError_t err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
         if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
         if (major != 10) { state.status = FA_STATUS_NO_SM100; return; }
-        err = cudaFuncSetAttribute(fa_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::kSmemBytes);
+        err = cudaDeviceGetAttribute(&state.sm_count, cudaDevAttrMultiProcessorCount, device);
+        if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
+        err = cudaFuncSetAttribute(fa_fwd_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg<64>::kSmemBytes);
         if (err == cudaSuccess)
-            err = cudaFuncSetAttribute(fa_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            err = cudaFuncSetAttribute(fa_fwd_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg<64>::kSmemBytes);
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(fa_fwd_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg<128>::kSmemBytes);
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(fa_fwd_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg<128>::kSmemBytes);
         if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
         // The warpgroup register split (setmaxnreg) waits forever if the CTA launched with
         // fewer registers than it hands out: refuse to launch such a build.
-        for (const void* func : {reinterpret_cast<const void*>(fa_fwd_kernel<64>),
-                                 reinterpret_cast<const void*>(fa_fwd_kernel<128>)}) {
+        for (const void* func : {reinterpret_cast<const void*>(fa_fwd_kernel<64, false>),
+                                 reinterpret_cast<const void*>(fa_fwd_kernel<64, true>),
+                                 reinterpret_cast<const void*>(fa_fwd_kernel<128, false>),
+                                 reinterpret_cast<const void*>(fa_fwd_kernel<128, true>)}) {
             cudaFuncAttributes attributes{};
             err = cudaFuncGetAttributes(&attributes, func);
             if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
@@ -770,12 +826,16 @@ int validate(const void* q, const void* k, const void* v, const void* o, int bat
 
 template <int D>
 int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-           const Params& params, long long slabs, cudaStream_t stream)
+           const Params& params, bool one_tile, long long slabs, cudaStream_t stream)
 {
-    const long long blocks = slabs * params.num_pairs;
+    const long long blocks = slabs * params.num_units;
     if (blocks <= 0) return FA_STATUS_OK;
     if (blocks > INT_MAX) return FA_STATUS_INVALID_ARGUMENT;
-    fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+    const unsigned grid = static_cast<unsigned>(blocks);
+    if (one_tile)
+        fa_fwd_kernel<D, true><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+    else
+        fa_fwd_kernel<D, false><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -796,16 +856,21 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     const MapSet* maps = nullptr;
     if ((status = lookup_maps(q, k, v, o, slabs, seq_len, head_dim, &maps)) != FA_STATUS_OK) return status;
 
+    const long long count = slab_end - slab_begin;
     Params params{};
     params.seq_len = seq_len;
-    params.num_pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
+    // Small-grid dispatch: a CTA normally takes a row pair (two Q tiles whose softmax phases
+    // overlap on one SM). When even one CTA per Q tile would leave SMs idle, each Q tile gets
+    // its own CTA instead: twice the CTAs, each with a shorter critical path.
+    const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
+    const bool single = count * pairs * kQTiles <= g_devices[device].sm_count;
+    params.num_units = single ? (seq_len + kBlockM - 1) / kBlockM : pairs;
     params.slab_begin = slab_begin;
     params.scale_log2 = fa_default_scale(head_dim) * 1.4426950408889634f;
     params.causal = causal ? 1 : 0;
     params.inject_stall = inject_stall;
     params.timeout_ns = timeout_ns;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const long long count = slab_end - slab_begin;
     params.num_slabs = count;
     {
         // Causal groups: as many slabs as keep the group's K and V within 32 MB of L2.
@@ -813,8 +878,8 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
         const long long by_l2 = kv_bytes > 0 ? (32LL << 20) / kv_bytes : count;
         params.chunk = static_cast<int>(std::max(1LL, std::min(count, by_l2)));
     }
-    return head_dim == 64 ? launch<64>(maps->q, maps->k, maps->v, maps->o, params, count, s)
-                          : launch<128>(maps->q, maps->k, maps->v, maps->o, params, count, s);
+    return head_dim == 64 ? launch<64>(maps->q, maps->k, maps->v, maps->o, params, single, count, s)
+                          : launch<128>(maps->q, maps->k, maps->v, maps->o, params, single, count, s);
 }
 
 }  // namespace
@@ -884,8 +949,8 @@ int fa_sm100_query(int head_dim, FaTilingInfo* info)
     if (err != cudaSuccess) return static_cast<int>(err);
     const int status = prepare_device(device);
     if (status != FA_STATUS_OK) return status;
-    const void* func = head_dim == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<64>)
-                                      : reinterpret_cast<const void*>(fa_fwd_kernel<128>);
+    const void* func = head_dim == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<64, false>)
+                                      : reinterpret_cast<const void*>(fa_fwd_kernel<128, false>);
     const int dynamic_bytes = head_dim == 64 ? Cfg<64>::kSmemBytes : Cfg<128>::kSmemBytes;
     cudaFuncAttributes attributes{};
     if ((err = cudaFuncGetAttributes(&attributes, func)) != cudaSuccess) return static_cast<int>(err);

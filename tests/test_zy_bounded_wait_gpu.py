@@ -12,13 +12,16 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_injected_stall_times_out_and_context_survives(oracle, cuda_device):
+# (1, 2, 256, 64) launches one 128-row Q tile per CTA (small grid); (3, 25, 256, 64) launches
+# row-pair CTAs (75 slabs x 1 pair x 2 tiles > 148 SMs).
+@pytest.mark.parametrize("b, h", [(1, 2), (3, 25)])
+def test_injected_stall_times_out_and_context_survives(oracle, cuda_device, b, h):
     import torch
     from cuda_fused_attention_b200 import STATUS_DEVICE_TIMEOUT, AttentionShape, device_status, \
         launch_attention_sm100
     from cuda_fused_attention_b200 import _lib
     lib = _lib.load()
-    b, h, n, d = 1, 2, 256, 64
+    n, d = 256, 64
     q, k, v = oracle.make_inputs(b, h, n, d)
     dev = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda_device) for x in (q, k, v)]
     o = torch.empty_like(dev[0])
