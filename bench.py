@@ -350,7 +350,8 @@ def run_ours(args):
     value = flops_step_total / (ms_step * 1e-3) / 1e12
     peak, peak_src = measured_peak()
     sustained = measured_sustained_peak()
-    # Dominant (only) kernel: fa_fwd_kernel<128>; per-launch algorithmic FLOPs / mean launch time.
+    # Dominant (only) kernel: the row-pair kernel fa_fwd_kernel<128, false>; per-launch algorithmic
+    # FLOPs / mean launch time.
     achieved = (flops_dense_local + flops_causal_local) / ((dense_ms + causal_ms) * 1e-3) / 1e12
     traffic = profile_traffic()
 
@@ -423,7 +424,7 @@ def run_ours(args):
                      # and power samples in "clocks"); cuBLAS measured under the same cap:
                      "sustained_peak": sustained,
                      "frac_vs_sustained": None if sustained is None else achieved / sustained,
-                     "kernel": "fa_sm100::fa_fwd_kernel<128>",
+                     "kernel": "fa_sm100::fa_fwd_kernel<128, false>",
                      "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
                      "traffic_note": None if traffic is None else traffic.get("note")},
         "cpu_baseline": cpu,
