@@ -23,7 +23,7 @@
 //     TMEM) only when one of its scores exceeds the base by a factor 2^16.
 //   * Causal: key tiles above the diagonal are never loaded or computed; only
 //     the diagonal tile(s) and a ragged tail tile take the element mask. Blocks
-//     run in groups of slabs sized to L2, heaviest row pairs first across a group.
+//     run in groups of slabs sized to L2, heaviest units first across a group.
 //   * Epilogue: O from TMEM, times 1/l, to bf16, into the (now free) Q tile of
 //     shared memory in the swizzled layout, then one TMA store per 64 columns.
 //
@@ -237,8 +237,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const int lane = threadIdx.x % 32;
 
     // ---- work item ---------------------------------------------------------------
-    // A unit is p.tile_span consecutive 128-row Q tiles of one slab: a row pair (256 rows),
-    // or one tile when the host found the grid of pairs too small to fill the GPU.
+    // A unit is a row pair (256 rows, two Q tiles) of one slab, or in the one-tile kernel a
+    // single 128-row Q tile.
     // Dense: slab-major (the CTAs of a slab run together and share its K/V through L2).
     // Causal: slabs in groups of p.chunk; within a group the units go heaviest first,
     // each unit for every slab of the group, so the longest CTAs of the last slabs do not
@@ -924,6 +924,8 @@ double fa_sm100_min_bytes(int batch, int heads, int seq_len, int head_dim)
     return 4.0 * static_cast<double>(batch) * heads * seq_len * head_dim * 2.0;
 }
 
+// Traffic model of the row-pair kernel. The one-tile kernel, which only small grids use,
+// fetches each K/V tile once per 128-row Q tile instead of once per pair.
 double fa_sm100_hbm_bytes(int batch, int heads, int seq_len, int head_dim, int causal)
 {
     const double element = 2.0;
