@@ -47,6 +47,9 @@ def parse_args():
                     help="B,H,N,D instead of config 5 (profiling and exploration; not the headline)")
     ap.add_argument("--mask", choices=["both", "dense", "causal"], default="both",
                     help="forwards per step (default: one dense + one causal)")
+    ap.add_argument("--gather", action="store_true",
+                    help="with N > 1, also time the optional all-gather of the O slices (NCCL), "
+                         "separately from the forward; reported under \"gather\"")
     return ap.parse_args()
 
 
@@ -391,6 +394,13 @@ def run_ours(args):
         lib.fa_sm100_release_staging()
         del hq, hk, hv, ho
 
+    # ---- the optional O gather, timed on its own (not part of the step) ----------------------
+    gather = None
+    if args.gather and world > 1:
+        from cuda_fused_attention_b200.sharded import SlabShard, time_gather
+        gather = time_gather(o, SlabShard(full, rank, world), iters=max(1, min(args.steps, 5)),
+                             warmup=max(1, min(args.warmup, 2)))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
@@ -432,6 +442,8 @@ def run_ours(args):
         "gpu_launches": len(masks) * args.steps * world,
         "clocks": clocks.summary(),
     }
+    if gather is not None:
+        line["gather"] = gather
     emit(line)
     return 0
 

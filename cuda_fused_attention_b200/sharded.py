@@ -88,6 +88,43 @@ def gather_slabs(o_local, shard, group=None):
     return torch.cat(parts).view(o_local.dtype)
 
 
+def time_gather(o_local, shard, iters=5, warmup=2, group=None):
+    """Time gather_slabs on its own (it is never inside the forward's timed region): the mean
+    time of `iters` gathers after `warmup` untimed ones, max over ranks, with CUDA events on
+    the current stream for device tensors and the host clock otherwise. Bandwidths follow the
+    NCCL convention for an all-gather: algbw = bytes of the gathered output / time,
+    busbw = algbw * (world - 1) / world (what each rank's links carry)."""
+    import time
+    import torch
+    import torch.distributed as dist
+    world = shard.world
+    on_gpu = o_local.is_cuda
+    for _ in range(warmup):
+        gather_slabs(o_local, shard, group)
+    if dist.is_initialized() and world > 1:
+        dist.barrier(group=group, device_ids=[o_local.device.index] if on_gpu else None)
+    if on_gpu:
+        torch.cuda.synchronize(o_local.device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            gather_slabs(o_local, shard, group)
+        end.record()
+        end.synchronize()
+        ms = start.elapsed_time(end) / iters
+    else:
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            gather_slabs(o_local, shard, group)
+        ms = (time.perf_counter() - t0) * 1e3 / iters
+    (ms,) = max_over_ranks([ms], device=o_local.device if on_gpu else None, group=group)
+    out_bytes = shard.shape.numel * o_local.element_size()
+    algbw = out_bytes / (ms * 1e-3) / 1e9
+    return {"ms": ms, "bytes": out_bytes, "algbw_GBps": algbw, "busbw_GBps": algbw * (world - 1) / world,
+            "ranks": world, "iters": iters, "collective": "all_gather_into_tensor (raw bytes, padded to the "
+            "largest shard) plus the unpadding copy"}
+
+
 def max_over_ranks(values, device=None, group=None):
     """Element-wise max of a list of floats across ranks (the timing reduction)."""
     import torch

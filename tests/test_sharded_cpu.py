@@ -43,7 +43,7 @@ def _worker(rank, world, port, mode, result_path):
     import torch.distributed as dist
     import fa_oracle
     from cuda_fused_attention_b200 import AttentionShape
-    from cuda_fused_attention_b200.sharded import SlabShard, gather_slabs, max_over_ranks
+    from cuda_fused_attention_b200.sharded import SlabShard, gather_slabs, max_over_ranks, time_gather
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     shape = AttentionShape(1, 5, 70, 64)
@@ -59,6 +59,13 @@ def _worker(rank, world, port, mode, result_path):
         dist.destroy_process_group()
         return                      # leaves between steps, never joins the gather
     try:
+        if mode == "time":
+            stats = time_gather(bits, shard, iters=3, warmup=1)
+            if rank == 0:
+                import json
+                with open(result_path, "w") as fh:
+                    json.dump(stats, fh)
+            return
         full = gather_slabs(bits, shard)
         (worst,) = max_over_ranks([float(rank + 1)])
         if rank == 0:
@@ -86,6 +93,15 @@ def _spawn(mode, tmp_path):
 def test_gather_and_timing_reduction_two_ranks(tmp_path):
     result = _spawn("gather", tmp_path)
     assert open(result).read() == "ok"
+
+
+def test_gather_timing_two_ranks(tmp_path):
+    """sharded.time_gather, the separately timed O gather that bench.py --gather reports."""
+    import json
+    stats = json.load(open(_spawn("time", tmp_path)))
+    assert stats["ranks"] == 2 and stats["iters"] == 3 and stats["ms"] > 0
+    assert stats["bytes"] == 1 * 5 * 70 * 64 * 2
+    assert abs(stats["busbw_GBps"] - stats["algbw_GBps"] / 2) < 1e-9
 
 
 def test_rank_leaving_early_surfaces_as_error(tmp_path):
