@@ -69,12 +69,18 @@ def forward_local(q_local, k_local, v_local, o_local, shard, causal, stream=None
 
 def gather_slabs(o_local, shard, group=None):
     """Collect every rank's O slice on every rank (all_gather); returns the full flat tensor on
-    all ranks. Slices are padded to the largest shard so the collective is uniform; every rank
-    must call this, in the same order, like any collective."""
+    all ranks. When the shards differ in size, slices are padded to the largest so that the
+    collective is uniform; every rank must call this, in the same order, like any collective."""
     import torch
     import torch.distributed as dist
     # Moved as raw bytes: bit-exact, and every backend (NCCL, gloo) supports uint8.
     local = o_local.reshape(-1).view(torch.uint8)
+    if shard.shape.slabs % shard.world == 0:
+        # Equal shards: gather straight from the slice into the output (no padding copy in,
+        # no unpadding copy out).
+        recv = torch.empty(local.numel() * shard.world, dtype=torch.uint8, device=o_local.device)
+        dist.all_gather_into_tensor(recv, local, group=group)
+        return recv.view(o_local.dtype)
     item = o_local.element_size()
     pad = shard.max_slabs * shard.slab_elems * item
     send = torch.zeros(pad, dtype=torch.uint8, device=o_local.device)
@@ -120,9 +126,12 @@ def time_gather(o_local, shard, iters=5, warmup=2, group=None):
     (ms,) = max_over_ranks([ms], device=o_local.device if on_gpu else None, group=group)
     out_bytes = shard.shape.numel * o_local.element_size()
     algbw = out_bytes / (ms * 1e-3) / 1e9
+    even = shard.shape.slabs % world == 0
     return {"ms": ms, "bytes": out_bytes, "algbw_GBps": algbw, "busbw_GBps": algbw * (world - 1) / world,
-            "ranks": world, "iters": iters, "collective": "all_gather_into_tensor (raw bytes, padded to the "
-            "largest shard) plus the unpadding copy"}
+            "ranks": world, "iters": iters,
+            "collective": "all_gather_into_tensor of raw bytes" + (
+                ", straight from each rank's slice" if even else
+                ", padded to the largest shard, plus the unpadding copy")}
 
 
 def max_over_ranks(values, device=None, group=None):

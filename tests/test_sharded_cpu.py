@@ -46,7 +46,7 @@ def _worker(rank, world, port, mode, result_path):
     from cuda_fused_attention_b200.sharded import SlabShard, gather_slabs, max_over_ranks, time_gather
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
-    shape = AttentionShape(1, 5, 70, 64)
+    shape = AttentionShape(1, 4 if mode == "gather_even" else 5, 70, 64)   # 2+2 or 3+2 slabs
     shard = SlabShard(shape, rank, world)
     q, k, v = fa_oracle.make_inputs(shape.batch, shape.heads, shape.seq_len, shape.head_dim)
     begin, end = shard.bounds
@@ -90,8 +90,9 @@ def _spawn(mode, tmp_path):
     return result
 
 
-def test_gather_and_timing_reduction_two_ranks(tmp_path):
-    result = _spawn("gather", tmp_path)
+@pytest.mark.parametrize("mode", ["gather", "gather_even"])
+def test_gather_and_timing_reduction_two_ranks(tmp_path, mode):
+    result = _spawn(mode, tmp_path)
     assert open(result).read() == "ok"
 
 

@@ -37,22 +37,23 @@ def _rank_main(rank, world, port, result_path):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=device)
     try:
-        shape = AttentionShape(3, 5, 1000, 128)            # 15 slabs: ranges of 8 and 7
-        q, k, v = fa_oracle.make_inputs(shape.batch, shape.heads, shape.seq_len, shape.head_dim)
-        full = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(device) for x in (q, k, v)]
-        shard = SlabShard(shape, rank, world)
-        local = [shard.local_view(t).contiguous() for t in full]
-        o_local = torch.empty_like(local[0])
-        for causal in (False, True):
-            forward_local(local[0], local[1], local[2], o_local, shard, causal)
-            gathered = gather_slabs(o_local, shard)
-            if rank == 0:
-                o_one = torch.empty_like(full[0])
-                launch_attention_sm100(full[0], full[1], full[2], o_one, shape, causal)
-                torch.cuda.synchronize()
-                same = torch.equal(gathered.view(torch.int16), o_one.view(torch.int16))
-                with open(result_path + f".{int(causal)}", "w") as fh:
-                    fh.write("ok" if same else "mismatch")
+        # 15 slabs: ranges of 8 and 7 (padded gather); 8 slabs: 4 and 4 (direct gather).
+        for shape in (AttentionShape(3, 5, 1000, 128), AttentionShape(2, 4, 1000, 128)):
+            q, k, v = fa_oracle.make_inputs(shape.batch, shape.heads, shape.seq_len, shape.head_dim)
+            full = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(device) for x in (q, k, v)]
+            shard = SlabShard(shape, rank, world)
+            local = [shard.local_view(t).contiguous() for t in full]
+            o_local = torch.empty_like(local[0])
+            for causal in (False, True):
+                forward_local(local[0], local[1], local[2], o_local, shard, causal)
+                gathered = gather_slabs(o_local, shard)
+                if rank == 0:
+                    o_one = torch.empty_like(full[0])
+                    launch_attention_sm100(full[0], full[1], full[2], o_one, shape, causal)
+                    torch.cuda.synchronize()
+                    same = torch.equal(gathered.view(torch.int16), o_one.view(torch.int16))
+                    with open(result_path + f".{shape.slabs}.{int(causal)}", "w") as fh:
+                        fh.write("ok" if same else "mismatch")
     finally:
         dist.destroy_process_group()
 
@@ -64,5 +65,6 @@ def test_two_gpu_shards_equal_one_gpu(tmp_path):
         pytest.skip("needs two GPUs")
     result = str(tmp_path / "sharded")
     mp.start_processes(_rank_main, args=(2, _free_port(), result), nprocs=2, start_method="spawn", join=True)
-    for causal in (0, 1):
-        assert open(f"{result}.{causal}").read() == "ok"
+    for slabs in (15, 8):
+        for causal in (0, 1):
+            assert open(f"{result}.{slabs}.{causal}").read() == "ok"
