@@ -53,18 +53,37 @@ void free_buffers(Staging& st)
     st.capacity = 0;
 }
 
+// Streams and events that were created are destroyed again, so a failed set-up leaves
+// nothing behind and the next call starts over cleanly.
+void destroy_streams(Staging& st)
+{
+    for (cudaStream_t* s : {&st.in, &st.compute, &st.out}) {
+        if (*s != nullptr) cudaStreamDestroy(*s);
+        *s = nullptr;
+    }
+    for (int b = 0; b < kBuffers; ++b) {
+        for (cudaEvent_t* e : {&st.loaded[b], &st.computed[b], &st.stored[b]}) {
+            if (*e != nullptr) cudaEventDestroy(*e);
+            *e = nullptr;
+        }
+    }
+}
+
 int ensure(Staging& st, size_t bytes)
 {
     if (!st.ready) {
-        if (cudaStreamCreateWithFlags(&st.in, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaStreamCreateWithFlags(&st.compute, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaStreamCreateWithFlags(&st.out, cudaStreamNonBlocking) != cudaSuccess)
+        bool created = cudaStreamCreateWithFlags(&st.in, cudaStreamNonBlocking) == cudaSuccess &&
+                       cudaStreamCreateWithFlags(&st.compute, cudaStreamNonBlocking) == cudaSuccess &&
+                       cudaStreamCreateWithFlags(&st.out, cudaStreamNonBlocking) == cudaSuccess;
+        for (int b = 0; created && b < kBuffers; ++b) {
+            created = cudaEventCreateWithFlags(&st.loaded[b], cudaEventDisableTiming) == cudaSuccess &&
+                      cudaEventCreateWithFlags(&st.computed[b], cudaEventDisableTiming) == cudaSuccess &&
+                      cudaEventCreateWithFlags(&st.stored[b], cudaEventDisableTiming) == cudaSuccess;
+        }
+        if (!created) {
+            destroy_streams(st);
+            cudaGetLastError();
             return FA_STATUS_HOST_ALLOC;
-        for (int b = 0; b < kBuffers; ++b) {
-            if (cudaEventCreateWithFlags(&st.loaded[b], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&st.computed[b], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&st.stored[b], cudaEventDisableTiming) != cudaSuccess)
-                return FA_STATUS_HOST_ALLOC;
         }
         st.ready = true;
     }
