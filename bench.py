@@ -216,6 +216,16 @@ def cpu_single_thread_configs():
     return out
 
 
+def cpu_extrapolation(tflops):
+    """One bench step (all slabs of config 5, one dense + one causal forward) at the sampled host
+    rate. Every slab of a mask is the same work, so this is exact by slab count, but it is an
+    extrapolation, not a measurement."""
+    b, h, n, d = (CONFIG[key] for key in ("batch", "heads", "seq_len", "head_dim"))
+    step_flops = 4.0 * b * h * d * (n * n + n * (n + 1) / 2.0)   # attention_flops, dense + causal
+    return {"step_s": step_flops / (tflops * 1e12), "step_flops": step_flops,
+            "note": "extrapolated by slab count from the sample (identical work per slab), not measured"}
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -248,6 +258,7 @@ def run_reference_arm(args):
         "impl": "reference",
         "config": {"workload": "BASELINE config 5 (16,32,8192,128) dense+causal, CPU sample", **CONFIG},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample,
+                         "extrapolated": cpu_extrapolation(value),
                          "single_thread": cpu_single_thread_configs()},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -408,6 +419,7 @@ def run_ours(args):
         cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
                "sample": f"{threads} whole (8192 x 128) slabs, one per host thread, alternating dense/causal, "
                          f"{s:.1f} s wall",
+               "extrapolated": cpu_extrapolation(f / s / 1e12),
                "single_thread": cpu_single_thread_configs()}
 
     if world > 1:

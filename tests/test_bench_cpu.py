@@ -67,3 +67,14 @@ def test_roofline_inputs():
     # At least Q, K and V of a config-5 launch are read once, and O is written (partly still in L2).
     minimum = 3 * 16 * 32 * 8192 * 128 * 2
     assert traffic["bytes_per_launch"] >= minimum
+
+
+def test_cpu_extrapolation_is_exact_by_flops():
+    bench = _bench()
+    from cuda_fused_attention_b200 import AttentionShape, attention_flops
+    full = AttentionShape(16, 32, 8192, 128)
+    want = attention_flops(full, False) + attention_flops(full, True)
+    e = bench.cpu_extrapolation(0.02)
+    assert e["step_flops"] == want
+    assert abs(e["step_s"] - want / 0.02e12) < 1e-9 * e["step_s"]
+    assert "not measured" in e["note"]
