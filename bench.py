@@ -12,9 +12,13 @@ rank runs the same kernel on its own range -- no collective on the data path
 max over ranks. TFLOP/s uses the reference's FLOP count (kernels/v0_unfused.cu:
 118-126: causal pairs N(N+1)/2).
 
-The reference arm (--impl reference) times the reference's own CPU FP64 oracle
-(benchmarks/bench_flash_attention.cu:105-145, compiled from its sources into
-oracle/_ref) on all host cores over a bounded sample of the same workload.
+After W warm-up steps the GPU arm runs untimed steps for --soak-s seconds, so the
+timed steps see the clock the GPU holds under its power limit at every N.
+
+The reference arm (--impl reference) times the reference's CPU FP64 oracle
+(benchmarks/bench_flash_attention.cu:105-145, as the oracle port that is pinned to
+it bit for bit) on all host cores over a bounded, balanced sample of the same
+workload: the same dense and causal rows of an (8192 x 128) slab on every thread.
 """
 import argparse
 import ctypes
@@ -47,6 +51,9 @@ def parse_args():
                     help="B,H,N,D instead of config 5 (profiling and exploration; not the headline)")
     ap.add_argument("--mask", choices=["both", "dense", "causal"], default="both",
                     help="forwards per step (default: one dense + one causal)")
+    ap.add_argument("--soak-s", type=float, default=3.0,
+                    help="untimed seconds of steps after the warm-up, so the timed steps run at the "
+                         "power-limited steady-state clock (0 = time right after the warm-up)")
     ap.add_argument("--gather", action="store_true",
                     help="with N > 1, also time the optional all-gather of the O slices (NCCL), "
                          "separately from the forward; reported under \"gather\"")
@@ -120,7 +127,7 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -132,10 +139,16 @@ class ClockSampler:
                 self.proc.kill()
             self.reader.join(timeout=2)
 
-    def summary(self):
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def summary(self, since=None):
+        """Median SM clock, power and the limit reasons seen, over the samples read at or after
+        `since` (time.monotonic(); None = all samples)."""
         sm, mx, reasons, power = [], None, set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        names = self.REASONS
+        for stamp, line in self.lines:
+            if since is not None and stamp < since:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 7:
                 continue
@@ -159,29 +172,61 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_reference_sample(threads, seq_len, head_dim, use_reference=True):
-    """One bounded sample of the workload on the host: `threads` whole slabs, one per thread,
-    alternating dense and causal. Returns (flops, seconds, kind)."""
+SAMPLE_ROWS = 512    # query rows per host thread per mask in one reference-arm step
+CPU_BASELINE_REPEATS = 4   # the GPU arm's cpu_baseline: this many reference-arm step samples
+
+
+def sample_rows(seq_len, rows, thread, threads):
+    """Query-row ranges of one host thread's share of the sample, dense and causal.
+
+    Dense: `rows` consecutive rows. Causal: two mirrored halves [a, a + rows/2) and
+    [N - a - rows/2, N - a), so that row r and row N-1-r (r+1 and N-r keys) pair up and every
+    thread's causal share is rows*(N+1)/2 query-key pairs, the mean of a causal slab. The
+    offset a spreads the threads over the first half of the slab."""
+    half = rows // 2
+    span = max(0, seq_len // 2 - half)
+    a = (thread * span) // max(1, threads)
+    dense = [(a, min(seq_len, a + rows))]
+    causal = [(a, a + half), (seq_len - a - half, seq_len - a)]
+    return dense, causal
+
+
+def pairs_in(ranges, seq_len, causal):
+    """Query-key pairs the oracle evaluates for the given row ranges."""
+    total = 0
+    for lo, hi in ranges:
+        if causal:
+            total += (hi * (hi + 1) - lo * (lo + 1)) // 2   # rows r in [lo, hi) see r+1 keys
+        else:
+            total += (hi - lo) * seq_len
+    return total
+
+
+def cpu_row_sample(threads, seq_len, head_dim, rows=SAMPLE_ROWS):
+    """One bounded, balanced sample of the workload on the host: every thread computes the same
+    amount of dense and causal work (sample_rows) of one (seq_len x head_dim) slab with the oracle
+    port (oracle/fa_oracle.cpp, the reference's reference_attention restated statement for
+    statement and pinned to it bit for bit). Returns (flops, seconds)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import fa_oracle
-    ref = fa_oracle.load_reference() if use_reference else None
-    kind = "reference" if ref is not None else "port"
     lib = fa_oracle.load()
-    count = seq_len * head_dim
-    base = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
+    q, k, v = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
     # A private copy of the slab per thread, so no two threads share cache lines.
-    slabs = [tuple(np.copy(x) for x in base) for _ in range(threads)]
-    outs = [np.empty(count, np.float64) for _ in range(threads)]
+    slabs = [tuple(np.copy(x) for x in (q, k, v)) for _ in range(threads)]
     P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    plans = [sample_rows(seq_len, rows, i, threads) for i in range(threads)]
+    flops = 0.0
+    for dense, causal in plans:
+        flops += 4.0 * head_dim * (pairs_in(dense, seq_len, False) + pairs_in(causal, seq_len, True))
 
     def work(i):
-        causal = i % 2
-        q, k, v = slabs[i]
-        if ref is not None:
-            ref.ref_reference_attention(P(q), P(k), P(v), P(outs[i]), 1, 1, seq_len, head_dim, causal)
-        else:
-            lib.fa_oracle_attention(P(q), P(k), P(v), P(outs[i]), 1, 1, seq_len, head_dim, causal)
+        q_, k_, v_ = slabs[i]
+        dense, causal = plans[i]
+        for ranges, mask in ((dense, 0), (causal, 1)):
+            for lo, hi in ranges:
+                out = np.empty((hi - lo) * head_dim, np.float64)
+                lib.fa_oracle_attention_rows(P(q_), P(k_), P(v_), P(out), seq_len, head_dim, mask, 0, lo, hi)
 
     pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
     t0 = time.perf_counter()
@@ -189,9 +234,42 @@ def cpu_reference_sample(threads, seq_len, head_dim, use_reference=True):
         t.start()
     for t in pool:
         t.join()
-    seconds = time.perf_counter() - t0
-    flops = sum(fa_oracle.attention_flops(1, 1, seq_len, head_dim, i % 2) for i in range(threads))
-    return flops, seconds, kind
+    return flops, time.perf_counter() - t0
+
+
+def cpu_port_vs_reference(threads, seq_len=1024, head_dim=128):
+    """The port's throughput against the reference's own reference_attention (compiled from its
+    sources into oracle/_ref) on the same whole slabs, one dense and one causal per thread:
+    {"reference_tflops", "port_tflops", "port_over_reference"}, or None without oracle/_ref."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import fa_oracle
+    ref = fa_oracle.load_reference()
+    if ref is None:
+        return None
+    lib = fa_oracle.load()
+    q, k, v = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
+    slabs = [tuple(np.copy(x) for x in (q, k, v)) for _ in range(threads)]
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    flops = threads * sum(fa_oracle.attention_flops(1, 1, seq_len, head_dim, c) for c in (0, 1))
+
+    def timed(fn):
+        def work(i):
+            out = np.empty(seq_len * head_dim, np.float64)
+            for causal in (0, 1):
+                fn(P(slabs[i][0]), P(slabs[i][1]), P(slabs[i][2]), P(out), 1, 1, seq_len, head_dim, causal)
+        pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+        t0 = time.perf_counter()
+        for t in pool:
+            t.start()
+        for t in pool:
+            t.join()
+        return flops / (time.perf_counter() - t0) / 1e12
+
+    reference = timed(ref.ref_reference_attention)
+    port = timed(lib.fa_oracle_attention)
+    return {"shape": [1, 1, seq_len, head_dim], "masks": "dense+causal", "threads": threads,
+            "reference_tflops": reference, "port_tflops": port, "port_over_reference": port / reference}
 
 
 def cpu_single_thread_configs():
@@ -233,6 +311,11 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def spread(rates):
+    return {"min": min(rates), "max": max(rates),
+            "stdev": statistics.stdev(rates) if len(rates) > 1 else 0.0}
+
+
 def run_reference_arm(args):
     rank, world, _ = env_rank()
     if rank != 0:
@@ -240,24 +323,28 @@ def run_reference_arm(args):
     threads = host_threads()
     n, d = CONFIG["seq_len"], CONFIG["head_dim"]
     for _ in range(args.warmup):   # warm-up on a reduced sample: the CPU has nothing to warm
-        cpu_reference_sample(min(threads, 4), 1024, d)
+        cpu_row_sample(threads, n, d, rows=32)
     flops = secs = 0.0
-    kind = "reference"
+    rates = []
     for _ in range(args.steps):
-        f, s, kind = cpu_reference_sample(threads, n, d)
+        f, s_ = cpu_row_sample(threads, n, d)
         flops += f
-        secs += s
+        secs += s_
+        rates.append(f / s_ / 1e12)
     value = flops / secs / 1e12
-    sample = (f"{threads} whole (N=8192, D=128) slabs per step, one per host thread, alternating dense/"
-              f"causal, reference_attention (bench_flash_attention.cu:105-145) compiled from the reference "
-              f"sources; warm-up steps used N=1024")
+    sample = (f"per step and host thread: {SAMPLE_ROWS} dense + {SAMPLE_ROWS} causal query rows (mirrored "
+              f"halves, mean causal cost) of one (N=8192, D=128) slab, the same work on every thread; "
+              f"oracle port of reference_attention (bench_flash_attention.cu:105-145); warm-up steps 32 rows")
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) bf16 (reference generator, seeds 11/22/33)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic N(0,1) bf16 (reference generator, seeds 11/22/33)",
         "impl": "reference",
         "config": {"workload": "BASELINE config 5 (16,32,8192,128) dense+causal, CPU sample", **CONFIG},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample,
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample,
+                         "spread_over_steps": spread(rates),
+                         "port_vs_reference": cpu_port_vs_reference(threads),
                          "extrapolated": cpu_extrapolation(value),
                          "single_thread": cpu_single_thread_configs()},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -267,6 +354,25 @@ def run_reference_arm(args):
 
 
 # ----------------------------------------------------------------------------- GPU arm
+def gpu_index(local_rank):
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return visible.split(",")[local_rank] if visible else str(local_rank)
+
+
+def clock_fields(summary):
+    """A clock summary as a fixed-length float list (for an all-gather across ranks)."""
+    bits = sum(1 << i for i, name in enumerate(ClockSampler.REASONS) if name in summary.get("reasons", []))
+    return [summary.get("sm_mhz") or 0.0, summary.get("sm_max_mhz") or 0.0, summary.get("power_w") or 0.0,
+            summary.get("power_max_w") or 0.0, float(summary.get("samples") or 0), float(bits)]
+
+
+def clock_summary_from_fields(fields):
+    sm, mx, power, power_max, samples, bits = fields
+    return {"sm_mhz": sm or None, "sm_max_mhz": mx or None, "power_w": power or None,
+            "power_max_w": power_max or None, "samples": int(samples),
+            "reasons": [name for i, name in enumerate(ClockSampler.REASONS) if int(bits) >> i & 1]}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -279,6 +385,9 @@ def run_ours(args):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
+        # Communicator set-up lines (rank, nranks, transport) go to stderr, as the record of
+        # which ranks took part; nothing of NCCL runs in the timed region.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=device)
 
@@ -291,6 +400,14 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
+
+    def gather_rows(values):
+        t = torch.tensor(values, dtype=torch.float64, device=device)
+        if world == 1:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [x.tolist() for x in out]
 
     lib = _lib.load()
     config = dict(CONFIG)
@@ -337,11 +454,23 @@ def run_ours(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[local_rank] \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local_rank)
-    barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(gpu_id) as clocks:
+    with ClockSampler(gpu_index(local_rank)) as clocks:
+        # Heat soak (untimed): keep stepping until the GPU has run for soak_s seconds, so that
+        # the timed steps run in the power-limited steady state at every N. Without it a rank's
+        # share of the timed steps can be shorter than the power limit's response (at N=8 the
+        # timed region is ~60 ms), and N would compare burst clocks against capped ones.
+        soak_steps = 0
+        t_soak = time.monotonic()
+        while time.monotonic() - t_soak < args.soak_s:
+            step()
+            soak_steps += 1
+            if soak_steps % 2 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        soak_s = time.monotonic() - t_soak
+        barrier()
+        torch.cuda.synchronize()
+        t_timed = time.monotonic()
         start.record(stream)
         for a, b, c in ev:
             a.record(stream)
@@ -353,7 +482,12 @@ def run_ours(args):
             c.record(stream)
         end.record(stream)
         torch.cuda.synchronize()
+        t_timed_end = time.monotonic()
     barrier()
+    # Clock samples from the last second of the soak through the end of the timed region: the
+    # timed region alone can be shorter than the 200 ms sampling period.
+    clock_window = max(t_soak, t_timed - 1.0)
+    my_clocks = clocks.summary(since=clock_window)
     total_ms = start.elapsed_time(end)
     dense_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
     causal_ms = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
@@ -361,6 +495,7 @@ def run_ours(args):
     if status != 0:
         raise RuntimeError(f"device status {status} ({word:#x}) after timing")
     ms_step, dense_ms_max, causal_ms_max = max_over_ranks([total_ms / args.steps, dense_ms, causal_ms])
+    per_rank_clocks = [clock_summary_from_fields(f) for f in gather_rows(clock_fields(my_clocks))]
     value = flops_step_total / (ms_step * 1e-3) / 1e12
     peak, peak_src = measured_peak()
     sustained = measured_sustained_peak()
@@ -368,6 +503,14 @@ def run_ours(args):
     # FLOPs / mean launch time.
     achieved = (flops_dense_local + flops_causal_local) / ((dense_ms + causal_ms) * 1e-3) / 1e12
     traffic = profile_traffic()
+    rank_mhz = [c["sm_mhz"] for c in per_rank_clocks if c["sm_mhz"]]
+    mean_mhz = statistics.mean(rank_mhz) if rank_mhz else None
+    clock_norm = None if mean_mhz is None else {
+        "sm_mhz_mean_of_rank_medians": mean_mhz,
+        "tflops_per_ghz_per_gpu": value / world / (mean_mhz / 1e3),
+        "ms_per_step_x_ghz": ms_step * mean_mhz / 1e3,
+        "note": "value and step time normalised by the SM clock the ranks ran at: compare these across N "
+                "to separate the design's scaling from clock differences"}
 
     # ---- end-to-end through the host-buffer C ABI (pinned host memory) --------------------
     e2e = None
@@ -379,6 +522,19 @@ def run_ours(args):
         hq.copy_(q)
         hk.copy_(k)
         hv.copy_(v)
+
+        # The PCIe link's rate for one tensor each way (pinned, CUDA events), for the bound below.
+        def link_gbs(dst, src):
+            dst.copy_(src, non_blocking=True)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src, non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            return src.numel() * src.element_size() / (a.elapsed_time(b) * 1e-3) / 1e9
+        h2d_gbs = link_gbs(o, hq)
+        d2h_gbs = link_gbs(ho, o)
 
         def host_step():
             for causal in masks:
@@ -394,14 +550,24 @@ def run_ours(args):
             host_step()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
         barrier()
-        (e2e_ms,) = max_over_ranks([e2e_ms])
+        (e2e_ms, h2d_min, d2h_min) = max_over_ranks([e2e_ms, -h2d_gbs, -d2h_gbs])
+        h2d_min, d2h_min = -h2d_min, -d2h_min
         tensor_bytes = full.numel * 2
+        h2d_bytes = len(masks) * 3 * tensor_bytes
+        d2h_bytes = len(masks) * tensor_bytes
+        # H2D and D2H overlap (separate copy engines), so the link bound of a step is the
+        # slower direction's bytes per GPU over that direction's measured rate.
+        link_ms = max(h2d_bytes / world / (h2d_min * 1e9), d2h_bytes / world / (d2h_min * 1e9)) * 1e3
         e2e = {"value": flops_step_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": len(masks) * 3 * tensor_bytes,
-               "d2h_bytes_per_step": len(masks) * tensor_bytes,
+               "h2d_bytes_per_step": h2d_bytes,
+               "d2h_bytes_per_step": d2h_bytes,
                "api": "fa_sm100_fwd_host (C ABI, pinned host buffers, H2D+forward+D2H per call; "
-                      "one dense and one causal call per step; bytes summed over ranks)"}
+                      "one dense and one causal call per step; bytes summed over ranks)",
+               "link": {"h2d_gbs": h2d_min, "d2h_gbs": d2h_min, "bound_ms_per_step": link_ms,
+                        "bound_tflops": flops_step_total / (link_ms * 1e-3) / 1e12,
+                        "note": "pinned copy rate of one tensor each way on this GPU's PCIe link (slowest rank); "
+                                "the step cannot beat its H2D bytes at that rate"}}
         lib.fa_sm100_release_staging()
         del hq, hk, hv, ho
 
@@ -414,12 +580,23 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # The reference arm's step sample (the same rows, the same threads), repeated.
         threads = host_threads()
-        f, s, kind = cpu_reference_sample(threads, n, d)
-        cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-               "sample": f"{threads} whole (8192 x 128) slabs, one per host thread, alternating dense/causal, "
-                         f"{s:.1f} s wall",
-               "extrapolated": cpu_extrapolation(f / s / 1e12),
+        flops = secs = 0.0
+        rates = []
+        for _ in range(CPU_BASELINE_REPEATS):
+            f, s_ = cpu_row_sample(threads, n, d)
+            flops += f
+            secs += s_
+            rates.append(f / s_ / 1e12)
+        cpu = {"value": flops / secs / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{CPU_BASELINE_REPEATS} x the reference arm's step sample: {SAMPLE_ROWS} dense + "
+                         f"{SAMPLE_ROWS} causal query rows (mirrored halves, mean causal cost) of one ({n} x {d}) "
+                         f"slab per host thread, the same work on every thread, oracle port of reference_attention; "
+                         f"{secs:.1f} s wall",
+               "spread_over_repeats": spread(rates),
+               "port_vs_reference": cpu_port_vs_reference(threads),
+               "extrapolated": cpu_extrapolation(flops / secs / 1e12),
                "single_thread": cpu_single_thread_configs()}
 
     if world > 1:
@@ -437,13 +614,16 @@ def run_ours(args):
                    **config, "global_batch": config["batch"],
                    "parallelism": f"slab-sharded x{world} (batch*heads split, no collective)",
                    "l2": "inputs larger than L2 (3 GiB of Q/K/V + 1 GiB O per forward)"},
+        "soak": {"seconds": soak_s, "steps": soak_steps,
+                 "note": "untimed steps after the warm-up so that every N is timed at the power-limited "
+                         "steady-state clock (rank 0's figures)"},
         "pct_of_bf16_peak": 100.0 * value / world / peak,
         "dense_tflops": (flops_dense_local * world / (dense_ms_max * 1e-3) / 1e12) if 0 in masks else None,
         "causal_tflops": (flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12) if 1 in masks else None,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src,
-                     # The kernel runs the GPU into its 1000 W cap within the timed region (clock
-                     # and power samples in "clocks"); cuBLAS measured under the same cap:
+                     # The kernel runs the GPU into its 1000 W cap (clock and power samples in
+                     # "clocks"); cuBLAS measured under the same cap:
                      "sustained_peak": sustained,
                      "frac_vs_sustained": None if sustained is None else achieved / sustained,
                      "kernel": "fa_sm100::fa_fwd_kernel<128, false>",
@@ -452,7 +632,8 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": len(masks) * args.steps * world,
-        "clocks": clocks.summary(),
+        "clocks": {**my_clocks, "window": "last 1 s of the soak + the timed region", "per_rank": per_rank_clocks},
+        "clock_normalised": clock_norm,
     }
     if gather is not None:
         line["gather"] = gather

@@ -53,6 +53,7 @@
 #include <mutex>
 
 #include "fa_sm100.h"
+#include "fa_sm100_internal.h"
 #include "fa_sm100_ptx.cuh"
 
 namespace fa_sm100 {
@@ -839,6 +840,10 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, 
     return static_cast<int>(cudaGetLastError());
 }
 
+// Test-only: a stall armed by fa_sm100_test_arm_stall for the next launch this host thread
+// makes, whichever entry point makes it (0 = none armed).
+thread_local unsigned long long t_armed_stall_ns = 0;
+
 int forward(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len, int head_dim,
             int causal, long long slab_begin, long long slab_end, void* stream, int inject_stall,
             unsigned long long timeout_ns)
@@ -856,6 +861,11 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     const MapSet* maps = nullptr;
     if ((status = lookup_maps(q, k, v, o, slabs, seq_len, head_dim, &maps)) != FA_STATUS_OK) return status;
 
+    if (inject_stall == 0 && t_armed_stall_ns != 0) {
+        inject_stall = 1;
+        timeout_ns = t_armed_stall_ns;
+        t_armed_stall_ns = 0;
+    }
     const long long count = slab_end - slab_begin;
     Params params{};
     params.seq_len = seq_len;
@@ -884,6 +894,26 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
 
 }  // namespace
 
+namespace fa_sm100_internal {
+
+int take_error_word(cudaStream_t stream, unsigned int* word)
+{
+    unsigned int value = 0;
+    cudaError_t err = cudaMemcpyFromSymbolAsync(&value, g_fa_error_word, sizeof(value), 0, cudaMemcpyDeviceToHost,
+                                                stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return static_cast<int>(err);
+    if (word != nullptr) *word = value;
+    if (value == 0) return FA_STATUS_OK;
+    const unsigned int zero = 0;
+    err = cudaMemcpyToSymbolAsync(g_fa_error_word, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return static_cast<int>(err);
+    return FA_STATUS_DEVICE_TIMEOUT;
+}
+
+}  // namespace fa_sm100_internal
+
 extern "C" {
 
 int fa_sm100_fwd(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len,
@@ -906,6 +936,13 @@ int fa_sm100_fwd_inject_stall(const void* q, const void* k, const void* v, void*
     if (timeout_ns == 0 || timeout_ns > kDefaultTimeoutNs) return FA_STATUS_INVALID_ARGUMENT;
     const long long slabs = (batch > 0 && heads > 0) ? static_cast<long long>(batch) * heads : 0;
     return forward(q, k, v, o, batch, heads, seq_len, head_dim, causal, 0, slabs, stream, 1, timeout_ns);
+}
+
+int fa_sm100_test_arm_stall(unsigned long long timeout_ns)
+{
+    if (timeout_ns == 0 || timeout_ns > kDefaultTimeoutNs) return FA_STATUS_INVALID_ARGUMENT;
+    t_armed_stall_ns = timeout_ns;
+    return FA_STATUS_OK;
 }
 
 int fa_sm100_supported(int head_dim) { return (head_dim == 64 || head_dim == 128) ? 1 : 0; }

@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "fa_sm100.h"
+#include "fa_sm100_internal.h"
 
 namespace {
 
@@ -166,7 +167,9 @@ int fa_sm100_fwd_host(const void* q_host, const void* k_host, const void* v_host
     if (sync_in != cudaSuccess) return static_cast<int>(sync_in);
     if (sync_compute != cudaSuccess) return static_cast<int>(sync_compute);
     if (sync_out != cudaSuccess) return static_cast<int>(sync_out);
-    return FA_STATUS_OK;
+    // A launch that gave up on a bounded wait left some of its O rows unwritten: report it
+    // instead of returning those rows as a result.
+    return fa_sm100_internal::take_error_word(st.compute, nullptr);
 }
 
 int fa_sm100_release_staging(void)

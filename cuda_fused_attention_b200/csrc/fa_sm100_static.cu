@@ -27,9 +27,16 @@
 //     before any stream capture begins.
 //   * Every call shares the one array and it keeps the last call's contents.
 //     Nothing in it needs to start at zero: each chunk's Q/K/V are copied in
-//     in full and the kernel writes every O element it copies out. Calls that
-//     overlap on the GPU (different streams or host threads at once) race on
-//     the array; serialise them.
+//     in full and a launch that completes writes every O element copied out.
+//     A launch that gives up on a bounded device-side wait does not; the call
+//     then returns FA_STATUS_DEVICE_TIMEOUT (it reads and clears the device
+//     error word after its final synchronisation), and o_host must not be
+//     used. Calls that overlap on the GPU (different streams or host threads
+//     at once) race on the array; serialise them.
+//   * Lazy module loading (CUDA's default) loads the module that holds the
+//     array, and so allocates its 32 MiB, at the first call's
+//     cudaGetSymbolAddress. A caller that forbids allocation after start-up
+//     makes one call (any size) at start-up; later calls allocate nothing.
 // =============================================================================
 #include <cuda_runtime.h>
 
@@ -38,6 +45,7 @@
 #include <mutex>
 
 #include "fa_sm100.h"
+#include "fa_sm100_internal.h"
 
 namespace {
 
@@ -127,7 +135,10 @@ int fa_sm100_fwd_host_static(const void* q_host, const void* k_host, const void*
     if (status != FA_STATUS_OK) return status;
     if (err != cudaSuccess) return static_cast<int>(err);
     if (sync != cudaSuccess) return static_cast<int>(sync);
-    return FA_STATUS_OK;
+    // A launch that gave up on a bounded wait did not write all of its O rows, so the
+    // array's O region may still hold an earlier call's output: report the timeout instead
+    // of returning that. Reading and clearing the word is two small copies, no allocation.
+    return fa_sm100_internal::take_error_word(s, nullptr);
 }
 
 }  // extern "C"

@@ -99,7 +99,11 @@ FA_API float fa_default_scale(int head_dim);
 /* Reads and clears the device-side error word of the current device after a
  * device synchronisation. FA_STATUS_OK, FA_STATUS_DEVICE_TIMEOUT, or a
  * cudaError_t from the synchronisation. `detail` (may be NULL) receives the raw
- * word: bit 0 set by any timeout, bits 8..15 the id of the wait that gave up. */
+ * word: bit 0 set by any timeout, bits 8..15 the id of the wait that gave up.
+ * There is one word per device, shared by every launch, stream and host thread
+ * on it: with concurrent callers, a timeout is reported to whichever caller
+ * reads the word first (this call, or fa_sm100_fwd_host /
+ * fa_sm100_fwd_host_static, which read and clear it after their own work). */
 FA_API int fa_sm100_device_status(unsigned int* detail);
 
 /* Human-readable text for a status code. */
@@ -114,10 +118,20 @@ FA_API int fa_sm100_fwd_inject_stall(const void* q, const void* k, const void* v
                               int batch, int heads, int seq_len, int head_dim, int causal,
                               unsigned long long timeout_ns, void* stream);
 
+/* Test-only: arms a stall (as in fa_sm100_fwd_inject_stall, with limit
+ * timeout_ns, at most one second) for the next forward launch that this host
+ * thread makes through any entry point, so that tests can check how the
+ * host-buffer entries report a device-side timeout. One-shot. No reference
+ * counterpart. */
+FA_API int fa_sm100_test_arm_stall(unsigned long long timeout_ns);
+
 /* End-to-end call with HOST buffers (pageable or pinned): copies Q/K/V in,
  * runs the forward pass and copies O out, pipelined over slab chunks on two
  * streams of the current device, then synchronises. Uses staging buffers that
  * the library allocates on first use and keeps (see fa_sm100_release_staging).
+ * If a launch gave up on a bounded device-side wait, the call returns
+ * FA_STATUS_DEVICE_TIMEOUT (it reads and clears the device error word) and
+ * o_host is incomplete.
  * No reference counterpart: the reference harness does these copies itself
  * (benchmarks/bench_flash_attention.cu:545-560). */
 FA_API int fa_sm100_fwd_host(const void* q_host, const void* k_host, const void* v_host, void* o_host,
@@ -135,8 +149,12 @@ FA_API int fa_sm100_release_staging(void);
  * else FA_STATUS_STATIC_TOO_LARGE. Runs on `stream` (NULL = legacy default)
  * and synchronises it. The first call on a device resolves the array's device
  * address (cudaGetSymbolAddress) with that device current: make it before any
- * stream capture. All calls share the array: calls that overlap on the GPU
- * race, so serialise them. */
+ * stream capture. Under lazy module loading (CUDA's default) that first call
+ * is also when the module holding the array is loaded, which allocates its
+ * 32 MiB: a caller that forbids allocation after start-up makes one call at
+ * start-up. A device-side timeout is returned as FA_STATUS_DEVICE_TIMEOUT
+ * (o_host is then not a result). All calls share the array: calls that
+ * overlap on the GPU race, so serialise them. */
 FA_API int fa_sm100_fwd_host_static(const void* q_host, const void* k_host, const void* v_host, void* o_host,
                                     int batch, int heads, int seq_len, int head_dim, int causal, void* stream);
 

@@ -37,11 +37,23 @@ class Accuracy(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+def reference_tree():
+    """The reference source tree used to build oracle/_ref: the REFERENCE environment variable,
+    else a `reference` directory beside the repository; None where neither exists (as on a
+    machine that only runs the prebuilt files)."""
+    candidates = [os.environ.get("REFERENCE"), os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for path in candidates:
+        if path and os.path.isfile(os.path.join(path, "benchmarks", "bench_flash_attention.cu")):
+            return os.path.abspath(path)
+    return None
+
+
 def build():
     """Compile liboracle.so (and the reference shim where the reference tree exists)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if os.path.isdir(os.environ.get("REFERENCE", "/root/reference")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    tree = reference_tree()
+    if tree is not None:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REFERENCE={tree}"], check=True)
 
 
 def load():

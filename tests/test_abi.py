@@ -96,10 +96,12 @@ def test_rejected_arguments_without_gpu(lib):
     assert lib.fa_sm100_fwd_inject_stall(fake, fake, fake, fake, 1, 2, 128, 64, 0, 0, None) == 1001
     assert lib.fa_sm100_fwd_host(None, fake, fake, fake, 1, 2, 128, 64, 0) == 1001
     assert lib.fa_sm100_fwd_host(fake, fake, fake, fake, 1, 2, 128, 80, 0) == 1002
+    assert lib.fa_sm100_test_arm_stall(0) == 1001
+    assert lib.fa_sm100_test_arm_stall(2_000_000_000) == 1001
 
 
 def test_status_strings(lib):
-    for code in (0, 1001, 1002, 1003, 1004, 1005, 1006, 1007, 1008, 1009):
+    for code in (0, 1001, 1002, 1003, 1004, 1005, 1006, 1007, 1008, 1009, 1010):
         assert lib.fa_sm100_status_string(code)
     assert b"unknown" in lib.fa_sm100_status_string(123456)
 

@@ -33,18 +33,42 @@ def test_stdout_carries_only_the_result_line():
 def test_clock_summary_parses_samples():
     bench = _bench()
     sampler = bench.ClockSampler(0)
-    sampler.lines = [
+    sampler.lines = [(float(i), line) for i, line in enumerate([
         "1965, 1965, 420.5, Not Active, Not Active, Not Active, Not Active",
         "1605, 1965, 995.1, Not Active, Not Active, Not Active, Active",
         "1590, 1965, 1002.3, Not Active, Not Active, Not Active, Active",
         "garbage line",
-    ]
+    ])]
     summary = sampler.summary()
     assert summary["samples"] == 3
     assert summary["sm_mhz"] == 1605 and summary["sm_max_mhz"] == 1965
     assert summary["reasons"] == ["sw_power_cap"]
     assert summary["power_w"] == 995.1 and summary["power_max_w"] == 1002.3
     assert bench.ClockSampler(0).summary()["samples"] == 0
+    # A window that starts at the second sample drops the idle first one.
+    late = sampler.summary(since=1.0)
+    assert late["samples"] == 2 and late["sm_mhz"] == (1605 + 1590) / 2
+    # Round trip through the fixed-length form the ranks all-gather.
+    back = bench.clock_summary_from_fields(bench.clock_fields(summary))
+    assert back["sm_mhz"] == 1605 and back["reasons"] == ["sw_power_cap"] and back["samples"] == 3
+
+
+def test_cpu_sample_gives_every_thread_the_same_work():
+    """Each host thread's share: `rows` dense rows and `rows` causal rows whose key counts average
+    to a causal slab's mean (N+1)/2, so no thread idles while another finishes."""
+    bench = _bench()
+    for n, rows, threads in ((8192, 1024, 16), (8192, 2048, 7), (1024, 64, 3)):
+        loads = set()
+        for t in range(threads):
+            dense, causal = bench.sample_rows(n, rows, t, threads)
+            assert all(0 <= lo < hi <= n for lo, hi in dense + causal)
+            # pairs_in against a direct count
+            direct_causal = sum(r + 1 for lo, hi in causal for r in range(lo, hi))
+            assert bench.pairs_in(causal, n, True) == direct_causal
+            assert bench.pairs_in(dense, n, False) == sum(hi - lo for lo, hi in dense) * n
+            assert direct_causal * 2 == rows * (n + 1)
+            loads.add((bench.pairs_in(dense, n, False), direct_causal))
+        assert len(loads) == 1
 
 
 def test_slab_ranges_cover_every_slab_once():

@@ -1,0 +1,59 @@
+"""The reference's correctness matrix on the sm_100a kernel, through the C ABI.
+
+kernels/ablation/experiments.cu:283-289 checks every variant on shape (1, 2, N, D) for
+N in {1,7,8,9,31,32,33,63,64,65,127,128,129,256}, D in {64,128}, dense and causal, and five
+input families (0 N(0,1); 1 all zeros; 2 all ones; 3 V[i] = (i mod D) - D/2; 4 Q and K x 4),
+against the CPU FP64 oracle with the gate "no non-finite output and max row-scale BF16 ULP
+<= 2.0". That is 280 cases; each runs here twice:
+
+* as (1, 2, N, D), which the launcher gives one 128-row Q tile per CTA (small grid), and
+* as the same two slabs repeated 38 times, (38, 2, N, D) = 76 slabs, large enough for the
+  row-pair CTAs; every slab must then match its oracle slab.
+
+Outputs are NaN-poisoned before each launch (stronger than the reference's zero fill).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2.0
+LENGTHS = (1, 7, 8, 9, 31, 32, 33, 63, 64, 65, 127, 128, 129, 256)
+REPEAT = 38
+
+
+def _run(dq, dk, dv, shape, causal):
+    import torch
+    from cuda_fused_attention_b200 import launch_attention_sm100
+    do = torch.empty_like(dq)
+    do.view(torch.int16).fill_(-1)
+    launch_attention_sm100(dq, dk, dv, do, shape, causal)
+    torch.cuda.synchronize()
+    return do.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_reference_correctness_matrix(oracle, cuda_device, d, causal):
+    import torch
+    from cuda_fused_attention_b200 import AttentionShape, device_status
+    worst = {}
+    for n in LENGTHS:
+        for family in range(5):
+            q, k, v = oracle.make_inputs(1, 2, n, d, family)
+            ref = oracle.attention(q, k, v, 1, 2, n, d, causal)
+            dev = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda_device) for x in (q, k, v)]
+            got = _run(*dev, AttentionShape(1, 2, n, d), causal)
+            acc = oracle.compare(got, ref, d, TOL)
+            assert acc["output_nan"] == 0 and acc["output_inf"] == 0, ("one tile", n, family, acc)
+            assert acc["passed"], ("one tile", n, family, acc)
+            tiled = [t.repeat(REPEAT) for t in dev]
+            got_pairs = _run(*tiled, AttentionShape(REPEAT, 2, n, d), causal)
+            acc_pairs = oracle.compare(got_pairs, np.tile(ref, REPEAT), d, TOL)
+            assert acc_pairs["output_nan"] == 0 and acc_pairs["output_inf"] == 0, ("row pairs", n, family)
+            assert acc_pairs["passed"], ("row pairs", n, family, acc_pairs)
+            key = family
+            worst[key] = max(worst.get(key, 0.0), acc["ulp"], acc_pairs["ulp"])
+    status, word = device_status()
+    assert status == 0 and word == 0
+    print(f"\nD={d} causal={causal}: worst row-scale ULP per input family {worst}")

@@ -4,10 +4,17 @@ Some callers cannot allocate device memory (code that must not call the
 allocator after start-up, processes whose device memory belongs to a pool or
 caching allocator). fa_sm100_fwd_host_static serves them by staging through a
 fixed file-scope __device__ array instead of cudaMalloc'd buffers. This file
-checks, through the C ABI, that two calls in a row (the second reusing the
-array the first left behind) give the same output as the existing entry
-points, and that the size limit is enforced. Collected last on purpose; it
-also passes alone in a fresh process.
+checks, through the C ABI:
+
+* calls in a row, each on different inputs than the call before (another mask
+  and input family), give the same output as the existing device entry point on
+  the same inputs, so output left in the array by an earlier call cannot pass;
+* after one call at start-up (which loads the module holding the array), the
+  following calls leave the device's free memory unchanged;
+* the size limit is enforced, and a device-side timeout is reported as a status
+  instead of returning stale output.
+
+Collected last on purpose; it also passes alone in a fresh process.
 """
 import ctypes
 
@@ -38,25 +45,71 @@ def test_static_entry_rejects_oversized_slab_before_any_cuda_call():
     assert lib.fa_sm100_static_staging_bytes() == 32 << 20
 
 
-@pytest.mark.gpu
-def test_static_entry_matches_existing_entry_twice(oracle, cuda_device):
+# (b, h, n, d, causal, family). Consecutive calls differ in mask and input family. The D=128
+# cases launch row-pair CTAs (36 slabs), the D=64 ones one Q tile per CTA (10 slabs); both
+# need several 8 MiB chunks of the array.
+CALLS = [(3, 12, 2048, 128, 1, 0), (3, 12, 2048, 128, 0, 4), (2, 5, 1500, 64, 0, 4), (2, 5, 1500, 64, 1, 3),
+         (3, 12, 2048, 128, 1, 0)]
+
+
+def _expected(oracle, cuda_device, b, h, n, d, causal, family):
+    """Inputs and the existing device entry's output on them (checked against the oracle)."""
     import torch
     from cuda_fused_attention_b200 import AttentionShape, launch_attention_sm100
+    q, k, v = oracle.make_inputs(b, h, n, d, family)
+    dev = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda_device) for x in (q, k, v)]
+    o = torch.empty_like(dev[0])
+    launch_attention_sm100(dev[0], dev[1], dev[2], o, AttentionShape(b, h, n, d), bool(causal))
+    torch.cuda.synchronize()
+    want = o.view(torch.int16).cpu().numpy().view(np.uint16)
+    ref = oracle.attention(q, k, v, b, h, n, d, causal)
+    assert oracle.compare(want, ref, d, TOL)["passed"]
+    return (q, k, v), want
+
+
+@pytest.mark.gpu
+def test_static_entry_matches_existing_entry_on_calls_in_a_row(oracle, cuda_device):
+    import torch
     lib = _lib()
-    cases = [(3, 6, 2048, 128, 1, 0), (2, 5, 1500, 64, 0, 4)]   # 36 and 10 slabs: several chunks each
-    for b, h, n, d, causal, family in cases:
-        q, k, v = oracle.make_inputs(b, h, n, d, family)
-        ref = oracle.attention(q, k, v, b, h, n, d, causal)
-        # The existing device entry on the same inputs.
-        dev = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda_device) for x in (q, k, v)]
-        o = torch.empty_like(dev[0])
-        launch_attention_sm100(dev[0], dev[1], dev[2], o, AttentionShape(b, h, n, d), bool(causal))
-        torch.cuda.synchronize()
-        want = o.view(torch.int16).cpu().numpy().view(np.uint16)
-        for call in range(2):                      # two calls in a row share the staging array
-            got = np.full_like(q, 0xFFFF)
-            rc = lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None)
-            assert rc == 0, (call, rc)
-            assert np.array_equal(got, want), (b, h, n, d, causal, call)
-            acc = oracle.compare(got, ref, d, TOL)
-            assert acc["passed"], (call, acc)
+    # Everything the device entry needs (inputs, its outputs, its kernels) exists before the
+    # allocation-free calls start, so the free-memory reading below sees only those calls.
+    cases = [(call, _expected(oracle, cuda_device, *call)) for call in CALLS]
+    outs = [np.empty_like(want) for _, (_, want) in cases]
+
+    def static_call(i):
+        (b, h, n, d, causal, _), ((q, k, v), want) = cases[i]
+        got = outs[i]
+        got.fill(0xFFFF)
+        rc = lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None)
+        assert rc == 0, (CALLS[i], rc)
+        assert np.array_equal(got, want), CALLS[i]
+
+    static_call(0)                       # start-up call: loads the module that holds the array
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for i in range(1, len(cases)):
+        static_call(i)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before, (free_before, free_after)
+
+
+@pytest.mark.gpu
+def test_static_entry_reports_device_timeout(oracle, cuda_device):
+    """A launch that gives up on a bounded wait (armed test stall, 20 ms) writes no O; the call
+    must return FA_STATUS_DEVICE_TIMEOUT rather than the array's previous contents as output,
+    and the next call must work normally."""
+    from cuda_fused_attention_b200 import STATUS_DEVICE_TIMEOUT, device_status
+    lib = _lib()
+    b, h, n, d, causal, family = 1, 2, 256, 64, 1, 0
+    (q, k, v), want = _expected(oracle, cuda_device, b, h, n, d, causal, family)
+    got = np.empty_like(want)
+    assert lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None) == 0
+    assert np.array_equal(got, want)     # the array's O region now holds this correct output
+    assert lib.fa_sm100_test_arm_stall(20_000_000) == 0
+    rc = lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None)
+    assert rc == STATUS_DEVICE_TIMEOUT
+    assert device_status() == (0, 0)     # the call read and cleared the word
+    got.fill(0xFFFF)
+    assert lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None) == 0
+    assert np.array_equal(got, want)
