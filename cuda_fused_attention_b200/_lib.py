@@ -37,8 +37,10 @@ SIGNATURES = {
     "fa_default_scale": (ctypes.c_float, [_I]),
     "fa_sm100_device_status": (_I, [ctypes.POINTER(ctypes.c_uint)]),
     "fa_sm100_status_string": (ctypes.c_char_p, [_I]),
+    "fa_sm100_debug_read": (_I, [_VP, ctypes.c_size_t]),
     "fa_sm100_fwd_inject_stall": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, ctypes.c_ulonglong, _VP]),
     "fa_sm100_test_arm_stall": (_I, [ctypes.c_ulonglong]),
+    "fa_sm100_test_force_kernel": (_I, [_I]),
     "fa_sm100_fwd_host": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I]),
     "fa_sm100_release_staging": (_I, []),
     "fa_sm100_fwd_host_static": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP]),

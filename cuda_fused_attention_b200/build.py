@@ -8,6 +8,10 @@ include/fa_sm100.h and the C++ API of include/flash_attention_sm100.h; the CUDA
 runtime is linked statically and the driver is reached only through
 cudaGetDriverEntryPoint, so the .so needs nothing but libc/libstdc++ and the
 NVIDIA driver at run time.
+
+The same sources compiled with FA_SM100_DEBUG_DUMP give lib/libfa_sm100_debug.so,
+whose kernel also dumps its intermediate tiles for layout checks
+(fa_sm100_debug_read); only tests load it.
 """
 import os
 import shutil
@@ -19,6 +23,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libfa_sm100.so")
+DEBUG_LIB_PATH = os.path.join(LIB_DIR, "libfa_sm100_debug.so")
 SOURCES = ["fa_sm100.cu", "fa_sm100_host.cu", "fa_sm100_api.cu", "fa_sm100_static.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -38,9 +43,9 @@ def compile_command(output=LIB_PATH, extra=()):
 
 
 def needs_build():
-    if not os.path.exists(LIB_PATH):
+    if not os.path.exists(LIB_PATH) or not os.path.exists(DEBUG_LIB_PATH):
         return True
-    lib_time = os.path.getmtime(LIB_PATH)
+    lib_time = min(os.path.getmtime(LIB_PATH), os.path.getmtime(DEBUG_LIB_PATH))
     deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
     deps += [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))]
     return any(os.path.getmtime(d) > lib_time for d in deps)
@@ -52,15 +57,22 @@ def build(force=False, verbose=True, ptxas_verbose=False):
         return LIB_PATH
     os.makedirs(LIB_DIR, exist_ok=True)
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-    cmd = compile_command(extra=extra)
-    if verbose:
-        print(" ".join(cmd), flush=True)
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if verbose or res.returncode != 0:
-        sys.stdout.write(res.stdout)
-        sys.stderr.write(res.stderr)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed with exit code {res.returncode}")
+    cmds = [compile_command(extra=extra),
+            compile_command(output=DEBUG_LIB_PATH, extra=["-DFA_SM100_DEBUG_DUMP"])]
+    procs = []
+    for cmd in cmds:
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append(subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True))
+    failed = 0
+    for proc in procs:
+        out, err = proc.communicate()
+        if verbose or proc.returncode != 0:
+            sys.stdout.write(out)
+            sys.stderr.write(err)
+        failed = failed or proc.returncode
+    if failed:
+        raise RuntimeError(f"nvcc failed with exit code {failed}")
     return LIB_PATH
 
 

@@ -78,7 +78,9 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunc
 // it; with a threshold of 8 instead, peaky rows (Q scaled by 4, config 3) made that
 // happen often enough to cost ~30 %.
 constexpr float kRescaleThreshold = 16.0f;
-constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemCols = 512;      // row-pair kernel: S0 | S1 | O0 | O1
+constexpr uint32_t kTmemColsOne = 256;   // one-tile kernel: S0 | O0
+
 constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
 
 // Wait-site ids recorded in the error word (bits 8..15).
@@ -140,6 +142,41 @@ struct Params {
 // timed out; bits 8..15: the site of the first recorded timeout.
 __device__ unsigned int g_fa_error_word;
 
+#ifdef FA_SM100_DEBUG_DUMP
+// Layout check of the tcgen05 data path (debug builds only, libfa_sm100_debug.so): CTA 0
+// writes what its Q tile 0 sees at each stage, so a test can check the stages one by one.
+// Float offsets (FA_SM100_DEBUG_* in fa_sm100.h):
+//   S [128][128]  QK^T of Q tile 0 and key tile 0 as loaded from TMEM (before scale and mask)
+//   P [128][128]  P of that tile as the PV MMA reads it from TMEM (bf16 widened to f32)
+//   O [128][128]  O of Q tile 0 after its last PV, before the 1/l scaling (D columns used)
+//   L [128]       row sum l;  M [128] final exponent base (running row max of raw scores)
+//   I [8]         slab, first query row, seq_len, head_dim, causal, one-tile kernel, key tiles, 1
+constexpr int kDbgS = 0;
+constexpr int kDbgP = kDbgS + 128 * 128;
+constexpr int kDbgO = kDbgP + 128 * 128;
+constexpr int kDbgL = kDbgO + 128 * 128;
+constexpr int kDbgM = kDbgL + 128;
+constexpr int kDbgInfo = kDbgM + 128;
+constexpr int kDbgFloats = kDbgInfo + 8;
+static_assert(kDbgFloats == FA_SM100_DEBUG_FLOATS, "debug dump layout");
+__device__ float g_fa_debug[kDbgFloats];
+
+// P columns [col0, col0 + 16 * chunks) of a row, read back from TMEM (packed bf16 pairs).
+__device__ __forceinline__ void debug_dump_p(uint32_t t_p, int row, int key0, int chunks32)
+{
+    for (int c = 0; c < chunks32; ++c) {
+        uint32_t w[32];
+        tmem_ld32(t_p + static_cast<uint32_t>(c * 32), w);
+        tmem_wait_ld();
+        reg_fence32(w);
+        for (int i = 0; i < 32; ++i) {
+            g_fa_debug[kDbgP + row * 128 + key0 + 64 * c + 2 * i] = __uint_as_float(w[i] << 16);
+            g_fa_debug[kDbgP + row * 128 + key0 + 64 * c + 2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+}
+#endif
+
 __device__ __forceinline__ void record_timeout(volatile uint32_t* abort_flag, uint32_t site)
 {
     *abort_flag = 1u;
@@ -179,6 +216,25 @@ __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, unsign
             return false;
         }
     }
+}
+
+// The exponent-base arithmetic, with every rounding explicit (never contracted into an
+// FMA, whatever the surrounding code lets the compiler fuse), so that both kernel
+// instantiations round a row identically. A row keeps its base until a half-tile maximum
+// exceeds it by kRescaleThreshold.
+__device__ __forceinline__ bool rebase_needed(float half_max, float row_max, float sl2)
+{
+    return __fmul_rn(__fsub_rn(half_max, row_max), sl2) > kRescaleThreshold;
+}
+
+__device__ __forceinline__ float rebase_alpha(float row_max, float m_new, float sl2)
+{
+    return ex2_approx(__fsub_rn(__fmul_rn(row_max, sl2), __fmul_rn(m_new, sl2)));
+}
+
+__device__ __forceinline__ float exp_base(float row_max, float sl2)
+{
+    return row_max == -INFINITY ? 0.0f : __fmul_rn(row_max, sl2);
 }
 
 // QK^T for one Q tile against one K tile: D/16 MMAs of M=128, N=128, K=16.
@@ -236,6 +292,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
+    // Tensor memory: S0 | S1 | O0 | O1, or S0 | O0 in the one-tile kernel.
+    constexpr uint32_t kCols = kOneTile ? kTmemColsOne : kTmemCols;
+    constexpr uint32_t kColO0 = kOneTile ? kBlockN : C::kColO0;
+    static_assert(!kOneTile || kColO0 + D <= kTmemColsOne, "one-tile TMEM budget");
 
     // ---- work item ---------------------------------------------------------------
     // A unit is a row pair (256 rows, two Q tiles) of one slab, or in the one-tile kernel a
@@ -282,7 +342,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         fence_mbarrier_init();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_alloc(smem_u32(tmem_slot), kCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -340,7 +400,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         if (lane == 0) {
             const uint32_t t_s0 = tmem_base + C::kColS0;
             const uint32_t t_s1 = tmem_base + C::kColS1;
-            const uint32_t t_o0 = tmem_base + C::kColO0;
+            const uint32_t t_o0 = tmem_base + kColO0;
             const uint32_t t_o1 = tmem_base + C::kColO1;
             const uint32_t sq0 = sq;
             const uint32_t sq1 = sq + C::kTileBytes;
@@ -445,7 +505,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const int r = quarter * 32 + lane;         // row within the Q tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const uint32_t t_s = lane_base + (t == 0 ? C::kColS0 : C::kColS1);
-        const uint32_t t_o = lane_base + (t == 0 ? C::kColO0 : C::kColO1);
+        const uint32_t t_o = lane_base + (t == 0 ? kColO0 : C::kColO1);
         const int row = q_row0 + t * kBlockM + r;            // query index in the slab
         const int limit = p.causal ? min(row, n - 1) : n - 1;  // last key this row attends to
         const int diag_tile = tile0 + t;                     // first key tile that needs the causal mask
@@ -532,6 +592,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             reg_fence32(s[1]);
             reg_fence32(s[2]);
             reg_fence32(s[3]);
+#ifdef FA_SM100_DEBUG_DUMP
+            if (blockIdx.x == 0 && j == 0 && t == 0)
+                for (int i = 0; i < 128; ++i) g_fa_debug[kDbgS + r * 128 + i] = __uint_as_float(s[i / 32][i % 32]);
+#endif
 
             const bool mask_tile = (p.causal && j >= diag_tile) || ((j + 1) * kBlockN > n);
             if (mask_tile) {
@@ -557,7 +621,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     mx[c] = fmaxf(a, b);
                 }
                 row_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                m_base = (row_max == -INFINITY) ? 0.0f : row_max * sl2;
+                m_base = exp_base(row_max, sl2);
             }
 
             float o_scale = 1.0f;    // O correction owed before the first PV of this tile reads O
@@ -570,13 +634,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 // Optimistic: the exponentials used the current base. If any score of this half
                 // exceeds it by more than the threshold (rare after the first tile), move the
                 // base, correct what was accumulated on the old one, and redo this half.
-                const bool need = (hmax - row_max) * sl2 > kRescaleThreshold;
+                const bool need = rebase_needed(hmax, row_max, sl2);
                 if (__any_sync(0xffffffffu, need)) {
                     const float m_new = need ? hmax : row_max;
-                    const float alpha = need ? ex2_approx(row_max * sl2 - m_new * sl2) : 1.0f;
-                    row_sum *= alpha;
+                    const float alpha = need ? rebase_alpha(row_max, m_new, sl2) : 1.0f;
+                    row_sum = __fmul_rn(row_sum, alpha);
                     row_max = m_new;
-                    m_base = (row_max == -INFINITY) ? 0.0f : row_max * sl2;
+                    m_base = exp_base(row_max, sl2);
                     if (h == 0) {
                         o_scale *= alpha;
                     } else {
@@ -591,7 +655,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     exp_half(s[2 * h], s[2 * h + 1], m_base, packed, hsum, hmax,
                          t_s + static_cast<uint32_t>(32 * h));
                 }
-                row_sum += hsum;
+                row_sum = __fadd_rn(row_sum, hsum);
                 // P of this half is in TMEM (stored by exp_half; a redo above stored it again).
                 if (h == 0) {
                     // Keys 0-63 of P are final: correct O first (the PV is the next reader of O;
@@ -604,6 +668,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
             if (!ok) break;
             tmem_wait_st();
+#ifdef FA_SM100_DEBUG_DUMP
+            if (blockIdx.x == 0 && j == 0 && t == 0) debug_dump_p(t_s, r, 0, 2);
+#endif
             tc_fence_before();
             mbar_arrive(bar(C::kBarPFull + t));
         }
@@ -622,6 +689,22 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
                 tmem_wait_ld();
                 reg_fence32(o);
+#ifdef FA_SM100_DEBUG_DUMP
+                if (blockIdx.x == 0 && t == 0) {
+                    for (int i = 0; i < 32; ++i) g_fa_debug[kDbgO + r * 128 + c * 32 + i] = __uint_as_float(o[i]);
+                    if (c == 0) {
+                        g_fa_debug[kDbgL + r] = row_sum;
+                        g_fa_debug[kDbgM + r] = row_max;
+                    }
+                    if (c == 0 && r == 0) {
+                        const float info[8] = {static_cast<float>(slab), static_cast<float>(q_row0),
+                                               static_cast<float>(n), static_cast<float>(D),
+                                               static_cast<float>(p.causal), kOneTile ? 1.0f : 0.0f,
+                                               static_cast<float>(n_kv), 1.0f};
+                        for (int i = 0; i < 8; ++i) g_fa_debug[kDbgInfo + i] = info[i];
+                    }
+                }
+#endif
                 uint32_t packed[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
@@ -646,7 +729,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                         tma_store_3d(&tm_o, stage + static_cast<uint32_t>(s * kSubBytes), s * 64,
                                      q_row0 + t * kBlockM, slab);
                     tma_store_commit();
-                    tma_store_wait_all();
+                    tma_store_wait_read_all();
                 }
             }
         }
@@ -660,7 +743,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        tmem_dealloc(tmem_base, kCols);
     }
 }
 
@@ -843,6 +926,9 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, 
 // Test-only: a stall armed by fa_sm100_test_arm_stall for the next launch this host thread
 // makes, whichever entry point makes it (0 = none armed).
 thread_local unsigned long long t_armed_stall_ns = 0;
+// Test-only: the kernel instantiation for this host thread's launches (fa_sm100_test_force_kernel):
+// 0 = the launcher's choice, 1 = one Q tile per CTA, 2 = row pairs.
+thread_local int t_forced_kernel = 0;
 
 int forward(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len, int head_dim,
             int causal, long long slab_begin, long long slab_end, void* stream, int inject_stall,
@@ -873,7 +959,8 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     // overlap on one SM). When even one CTA per Q tile would leave SMs idle, each Q tile gets
     // its own CTA instead: twice the CTAs, each with a shorter critical path.
     const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
-    const bool single = count * pairs * kQTiles <= g_devices[device].sm_count;
+    bool single = count * pairs * kQTiles <= g_devices[device].sm_count;
+    if (t_forced_kernel != 0) single = t_forced_kernel == 1;
     params.num_units = single ? (seq_len + kBlockM - 1) / kBlockM : pairs;
     params.slab_begin = slab_begin;
     params.scale_log2 = fa_default_scale(head_dim) * 1.4426950408889634f;
@@ -942,6 +1029,13 @@ int fa_sm100_test_arm_stall(unsigned long long timeout_ns)
 {
     if (timeout_ns == 0 || timeout_ns > kDefaultTimeoutNs) return FA_STATUS_INVALID_ARGUMENT;
     t_armed_stall_ns = timeout_ns;
+    return FA_STATUS_OK;
+}
+
+int fa_sm100_test_force_kernel(int kind)
+{
+    if (kind < 0 || kind > 2) return FA_STATUS_INVALID_ARGUMENT;
+    t_forced_kernel = kind;
     return FA_STATUS_OK;
 }
 
@@ -1023,6 +1117,20 @@ int fa_sm100_device_status(unsigned int* detail)
     if (err != cudaSuccess) return static_cast<int>(err);
     if (detail != nullptr) *detail = word;
     return word ? FA_STATUS_DEVICE_TIMEOUT : FA_STATUS_OK;
+}
+
+int fa_sm100_debug_read(float* out, size_t floats)
+{
+#ifdef FA_SM100_DEBUG_DUMP
+    if (out == nullptr || floats < static_cast<size_t>(kDbgFloats)) return FA_STATUS_INVALID_ARGUMENT;
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpyFromSymbol(out, g_fa_debug, sizeof(float) * kDbgFloats);
+    return static_cast<int>(err);
+#else
+    (void)out;
+    (void)floats;
+    return FA_STATUS_UNSUPPORTED;
+#endif
 }
 
 const char* fa_sm100_status_string(int status)

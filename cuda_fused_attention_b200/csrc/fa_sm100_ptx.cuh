@@ -97,9 +97,12 @@ __device__ __forceinline__ void tma_store_commit()
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_store_wait_all()
+// Waits until every committed bulk store has finished READING its shared-memory
+// source (the smem may then be reused or released; the global writes complete on
+// their own and are visible to later work on the stream once the grid finishes).
+__device__ __forceinline__ void tma_store_wait_read_all()
 {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA store).

@@ -106,6 +106,28 @@ FA_API float fa_default_scale(int head_dim);
  * fa_sm100_fwd_host_static, which read and clear it after their own work). */
 FA_API int fa_sm100_device_status(unsigned int* detail);
 
+/* Debug builds only (libfa_sm100_debug.so, compiled with FA_SM100_DEBUG_DUMP; the
+ * counterpart of the reference's FA_V3_DEBUG_DUMP option, kernels/v3/v3_tensorcore.cu:
+ * 101, :189-204, :680-709): CTA 0 of each launch writes what its first Q tile sees at
+ * each stage of the tcgen05 path, and this call copies the last launch's dump to `out`
+ * (FA_SM100_DEBUG_FLOATS floats, row major):
+ *   [FA_SM100_DEBUG_S + 128*r + k]  QK^T of query row r of the tile and key k of key tile 0,
+ *                                   as loaded from TMEM, before scale and mask
+ *   [FA_SM100_DEBUG_P + 128*r + k]  P of the same element as the PV MMA reads it (bf16 -> f32)
+ *   [FA_SM100_DEBUG_O + 128*r + d]  O after the last PV, before the 1/l scaling
+ *   [FA_SM100_DEBUG_L + r]          row sum l;  [FA_SM100_DEBUG_M + r] final row max
+ *   [FA_SM100_DEBUG_INFO + 0..7]    slab, first query row of the tile, seq_len, head_dim,
+ *                                   causal, one-tile kernel (0/1), key tiles, 1
+ * The product library returns FA_STATUS_UNSUPPORTED. */
+#define FA_SM100_DEBUG_S      0
+#define FA_SM100_DEBUG_P      16384
+#define FA_SM100_DEBUG_O      32768
+#define FA_SM100_DEBUG_L      49152
+#define FA_SM100_DEBUG_M      49280
+#define FA_SM100_DEBUG_INFO   49408
+#define FA_SM100_DEBUG_FLOATS 49416
+FA_API int fa_sm100_debug_read(float* out, size_t floats);
+
 /* Human-readable text for a status code. */
 FA_API const char* fa_sm100_status_string(int status);
 
@@ -124,6 +146,12 @@ FA_API int fa_sm100_fwd_inject_stall(const void* q, const void* k, const void* v
  * host-buffer entries report a device-side timeout. One-shot. No reference
  * counterpart. */
 FA_API int fa_sm100_test_arm_stall(unsigned long long timeout_ns);
+
+/* Test-only: which kernel instantiation this host thread's launches use -- 0 the
+ * launcher's own choice (the default), 1 one 128-row Q tile per CTA, 2 a row pair
+ * (two Q tiles) per CTA -- so that tests can run both on the same shapes. Stays set
+ * until changed. No reference counterpart. */
+FA_API int fa_sm100_test_force_kernel(int kind);
 
 /* End-to-end call with HOST buffers (pageable or pinned): copies Q/K/V in,
  * runs the forward pass and copies O out, pipelined over slab chunks on two

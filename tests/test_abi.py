@@ -98,6 +98,8 @@ def test_rejected_arguments_without_gpu(lib):
     assert lib.fa_sm100_fwd_host(fake, fake, fake, fake, 1, 2, 128, 80, 0) == 1002
     assert lib.fa_sm100_test_arm_stall(0) == 1001
     assert lib.fa_sm100_test_arm_stall(2_000_000_000) == 1001
+    assert lib.fa_sm100_test_force_kernel(3) == 1001
+    assert lib.fa_sm100_test_force_kernel(0) == 0
 
 
 def test_status_strings(lib):

@@ -350,3 +350,27 @@ def test_query_reports_resources(cuda_device):
         assert info["rows_per_block"] == 256 and info["max_blocks_per_sm"] == 1
         assert info["local_bytes_per_thread"] < 64
     assert query_sm100(96)["supported"] == 0
+
+
+def test_one_tile_kernel_equals_row_pair_kernel(oracle, cuda_device):
+    """The two instantiations give the same bits for every row, whatever the launcher picks:
+    the one-tile kernel spreads a row over two threads but keeps the row-pair kernel's
+    arithmetic (same base decisions, same summation order). Forced on the same shapes,
+    including the x4 families, whose peaky rows move the exponent base on either half of a
+    tile; and a slab's output does not depend on how many slabs share its launch."""
+    import torch
+    from cuda_fused_attention_b200 import AttentionShape, _lib
+    lib = _lib.load()
+    try:
+        for (b, h, n, d) in [(2, 5, 1500, 64), (3, 4, 1000, 128), (1, 3, 4096, 128), (2, 2, 300, 64)]:
+            for family in (0, 4, 5):
+                q, k, v = oracle.make_inputs(b, h, n, d, family)
+                for causal in (0, 1):
+                    outs = []
+                    for kind in (1, 2):
+                        assert lib.fa_sm100_test_force_kernel(kind) == 0
+                        outs.append(run_kernel(q, k, v, AttentionShape(b, h, n, d), causal, cuda_device))
+                    assert np.array_equal(outs[0], outs[1]), (b, h, n, d, family, causal)
+        check_device_clean()
+    finally:
+        lib.fa_sm100_test_force_kernel(0)
