@@ -41,6 +41,7 @@ SIGNATURES = {
     "fa_sm100_fwd_inject_stall": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, ctypes.c_ulonglong, _VP]),
     "fa_sm100_test_arm_stall": (_I, [ctypes.c_ulonglong]),
     "fa_sm100_test_force_kernel": (_I, [_I]),
+    "fa_sm100_test_force_split": (_I, [_I]),
     "fa_sm100_fwd_host": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I]),
     "fa_sm100_release_staging": (_I, []),
     "fa_sm100_fwd_host_static": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP]),

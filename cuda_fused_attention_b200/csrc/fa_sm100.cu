@@ -49,6 +49,7 @@
 #include <climits>
 #include <cmath>
 #include <cstdint>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
 
@@ -82,17 +83,21 @@ constexpr uint32_t kTmemCols = 512;      // row-pair kernel: S0 | S1 | O0 | O1
 constexpr uint32_t kTmemColsOne = 256;   // one-tile kernel: S0 | O0
 
 constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
+constexpr int kMaxChunks = 64;              // key-range split: chunks per unit at most
 
 // Wait-site ids recorded in the error word (bits 8..15).
 enum WaitSite : uint32_t {
     kSiteMmaQ = 1, kSiteMmaK = 2, kSiteMmaV = 3, kSiteMmaP0 = 4, kSiteMmaP1 = 5,
     kSiteLoadEmpty = 6, kSiteSoftS = 7, kSiteSoftO = 8, kSiteEpilogue = 9, kSiteInjected = 10,
-    kSiteDrain = 11,
+    kSiteDrain = 11, kSitePartial = 12,
 };
 
 template <int D>
 struct Cfg {
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    // A split partial of one Q tile: O as [D/4 column groups][128 rows] of float4 (a warp's 32
+    // rows of one column group are 512 contiguous bytes), then the 128 row maxima and sums.
+    static constexpr int kPartTileFloats = D * kBlockM + 2 * kBlockM;
     static constexpr int kSub = D / 64;                       // swizzle blocks per row
     static constexpr int kTileBytes = kSub * kSubBytes;       // one Q, K or V tile
     static constexpr int kStages = (D == 128) ? 4 : 8;        // K/V ring slots
@@ -112,9 +117,12 @@ struct Cfg {
     static constexpr int kBarEpi = kBarOFull + 2;
     static constexpr int kBarDrain = kBarEpi + 2;
     static constexpr int kBarNever = kBarDrain + 1;
-    static constexpr int kNumBars = kBarNever + 1;
-    static constexpr int kMiscOff = kBarOff + kNumBars * 8;   // tmem base (u32), abort flag (u32)
-    static constexpr int kSmemUsed = kMiscOff + 16;
+    static constexpr int kBarPart = kBarNever + 1;        // split: all softmax threads wrote their partial rows
+    static constexpr int kBarPartDone = kBarPart + 1;     // split: this chunk has been counted in
+    static constexpr int kNumBars = kBarPartDone + 1;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;   // tmem base, abort flag, last-chunk flag (u32)
+    static constexpr int kItemOff = kMiscOff + 16;            // the CTA's work item (WorkItem), for the epilogue
+    static constexpr int kSmemUsed = kItemOff + 32;
     static constexpr int kSmemBytes = kSmemUsed + 1024;       // slack for 1024-byte alignment
     static constexpr uint32_t kColS0 = 0;
     static constexpr uint32_t kColS1 = kBlockN;
@@ -124,6 +132,19 @@ struct Cfg {
     static constexpr uint32_t kIdescPV = make_idesc_bf16(kBlockM, D, true);
     static_assert(kColO1 + D <= kTmemCols, "TMEM budget");
     static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// A CTA's work item as decoded at kernel start; kept in shared memory so that the values only
+// the epilogue needs do not occupy registers through the main loop.
+struct WorkItem {
+    int slab_local;     // slab within this launch
+    int unit;           // row pair (or Q tile in the one-tile kernel) of the slab
+    int chunk;          // chunk of the unit's key range
+    int nchunks;        // chunks the unit's key range is split into (1 = not split)
+    int item_first;     // work item of the unit's chunk 0 (indexes the partials)
+    int kv_begin;       // first key tile of this CTA
+    int n_kv;           // key tiles of this CTA
+    int pad;
 };
 
 struct Params {
@@ -136,6 +157,13 @@ struct Params {
     unsigned long long timeout_ns;
     long long num_slabs;        // slabs in this launch
     int chunk;                  // causal block order: slabs per group (see the kernel's work item)
+    // Causal key-range split (0 = none): a unit with more than split_len key tiles is processed
+    // by ceil(tiles / split_len) CTAs ("chunks"), each over a contiguous range of its key tiles;
+    // every chunk writes an unnormalised partial and the last to finish merges them.
+    int split_len;
+    int items;                  // work items per slab: units, or chunks when split
+    float* partial;             // [slabs * items][Q tiles][Cfg::kPartTileFloats] (split only)
+    unsigned int* counters;     // [slabs * num_units] chunks done per unit, zero at launch (split only)
 };
 
 // Device error word of this module instance (one per device). Bit 0: some wait
@@ -288,6 +316,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const uint32_t bars = base + C::kBarOff;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMiscOff + 4);
+    volatile uint32_t* last_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMiscOff + 8);
     auto bar = [&](int index) -> uint32_t { return bars + static_cast<uint32_t>(index) * 8u; };
 
     const int warp = threadIdx.x / 32;
@@ -305,29 +334,77 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     // each unit for every slab of the group, so the longest CTAs of the last slabs do not
     // start late and stretch the tail, while the K/V of only one group (sized on the host
     // to a fraction of L2) is being read at a time.
+    constexpr bool two = !kOneTile;                      // a second Q tile in this CTA
+    const int n = p.seq_len;
+    const int kv_tiles_all = (n + kBlockN - 1) / kBlockN;
+    // Key tiles a unit attends to, and the chunks its key range is split into.
+    auto unit_tiles = [&](int u) -> int {
+        const int t0 = u * (two ? kQTiles : 1);
+        return p.causal ? min(kv_tiles_all, t0 + (two ? 2 : 1)) : kv_tiles_all;
+    };
+    auto unit_chunks = [&](int u) -> int {
+        return p.split_len > 0 ? (unit_tiles(u) + p.split_len - 1) / p.split_len : 1;
+    };
     const long long block = blockIdx.x;
     long long slab_local;
     int unit;
+    int chunk = 0, nchunks = 1;
+    long long item_first = 0;   // split: the work item of chunk 0 of this unit
     if (p.causal) {
-        const long long per_group = static_cast<long long>(p.chunk) * p.num_units;
+        const long long per_group = static_cast<long long>(p.chunk) * p.items;
         const long long group = block / per_group;
         const long long first = group * p.chunk;
         const long long in_group = min(static_cast<long long>(p.chunk), p.num_slabs - first);
         const long long within = block - group * per_group;
         const long long level = within / in_group;
         slab_local = first + (within - level * in_group);
-        unit = p.num_units - 1 - static_cast<int>(level);
+        if (two && p.split_len > 0) {
+            // Items of a slab: units heaviest first, each unit's chunks in key order (the split
+            // is a row-pair-kernel feature; the host never asks the one-tile kernel for it).
+            int item = static_cast<int>(level);
+            unit = 0;
+            for (int u = p.num_units - 1; u >= 0; --u) {
+                const int ncu = unit_chunks(u);
+                if (item < ncu || u == 0) {
+                    unit = u;
+                    nchunks = ncu;
+                    chunk = min(item, ncu - 1);
+                    break;
+                }
+                item -= ncu;
+            }
+            item_first = level - chunk;
+        } else {
+            unit = p.num_units - 1 - static_cast<int>(level);
+        }
     } else {
         slab_local = block / p.num_units;
         unit = static_cast<int>(block - slab_local * p.num_units);
     }
     const int slab = static_cast<int>(p.slab_begin + slab_local);
-    constexpr bool two = !kOneTile;                      // a second Q tile in this CTA
     const int tile0 = unit * (two ? kQTiles : 1);        // first 128-row Q tile of this CTA
+    // Fields of the work item in shared memory, read through their 32-bit shared addresses.
+    auto item_field = [&](int offset) -> int {
+        int value;
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(value) : "r"(base + C::kItemOff + static_cast<uint32_t>(offset)));
+        return value;
+    };
     const int q_row0 = tile0 * kBlockM;
-    const int n = p.seq_len;
-    const int kv_tiles_all = (n + kBlockN - 1) / kBlockN;
-    const int n_kv = p.causal ? min(kv_tiles_all, tile0 + (two ? 2 : 1)) : kv_tiles_all;
+    const int tiles = unit_tiles(unit);
+    // Chunk c of a unit covers key tiles [c * tiles / nchunks, (c + 1) * tiles / nchunks) (32-bit: the
+    // host splits only units with at most kMaxChunks chunks, so c * tiles < 2^31).
+    const int kv_begin_0 = chunk * tiles / nchunks;
+    const int n_kv_0 = (chunk + 1) * tiles / nchunks - kv_begin_0;
+    if (two && threadIdx.x == 0) {
+        WorkItem* item_smem = reinterpret_cast<WorkItem*>(smem + C::kItemOff);
+        item_smem->slab_local = static_cast<int>(slab_local);
+        item_smem->unit = unit;
+        item_smem->chunk = chunk;
+        item_smem->nchunks = nchunks;
+        item_smem->item_first = static_cast<int>(item_first);
+        item_smem->kv_begin = kv_begin_0;
+        item_smem->n_kv = n_kv_0;
+    }
 
     // ---- set-up ---------------------------------------------------------------
     // Barrier set-up, one barrier per lane of warp 0: p_half, p_full and epi count the 128
@@ -336,7 +413,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     if (warp == 0) {
         for (int b = lane; b < C::kNumBars; b += 32) {
             const bool per_thread = (b >= C::kBarPHalf && b < C::kBarPvHalf) || (b >= C::kBarEpi && b < C::kBarDrain);
-            mbar_init(bar(b), per_thread ? kBlockM : 1);
+            const uint32_t count = b == C::kBarPart ? (kOneTile ? kBlockM : kRowsPerCta) : (per_thread ? kBlockM : 1);
+            mbar_init(bar(b), count);
         }
         if (lane == 0) *abort_flag = 0u;
         fence_mbarrier_init();
@@ -349,6 +427,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Key tiles of this CTA: [kv_begin, kv_begin + n_kv) (loaded where each role starts).
+    const int kv_begin = two ? item_field(offsetof(WorkItem, kv_begin)) : 0;
+    const int n_kv = two ? item_field(offsetof(WorkItem, n_kv)) : n_kv_0;
     const unsigned long long timeout = p.timeout_ns;
 
     if (warp == kLoadWarp) {
@@ -378,7 +459,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 }
                 mbar_arrive_expect_tx(bar(C::kBarKvFull + slot), C::kTileBytes);
                 const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
-                const int key0 = (i >> 1) * kBlockN;
+                const int key0 = (kv_begin + (i >> 1)) * kBlockN;
 #pragma unroll
                 for (int s = 0; s < C::kSub; ++s)
                     tma_load_3d(ring + slot * C::kTileBytes + s * kSubBytes, map, bar(C::kBarKvFull + slot),
@@ -508,7 +589,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const uint32_t t_o = lane_base + (t == 0 ? kColO0 : C::kColO1);
         const int row = q_row0 + t * kBlockM + r;            // query index in the slab
         const int limit = p.causal ? min(row, n - 1) : n - 1;  // last key this row attends to
-        const int diag_tile = tile0 + t;                     // first key tile that needs the causal mask
+        // Local key-tile indices from which a tile needs the element mask: the causal diagonal,
+        // and the first tile that reaches past N.
+        const int diag_local = tile0 + t - kv_begin;
+        const int tail_local = n / kBlockN - kv_begin;
         const float sl2 = p.scale_log2;
 
         float row_max = -INFINITY;   // running max of raw scores
@@ -597,9 +681,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 for (int i = 0; i < 128; ++i) g_fa_debug[kDbgS + r * 128 + i] = __uint_as_float(s[i / 32][i % 32]);
 #endif
 
-            const bool mask_tile = (p.causal && j >= diag_tile) || ((j + 1) * kBlockN > n);
+            const bool mask_tile = (p.causal && j >= diag_local) || j >= tail_local;
             if (mask_tile) {
-                const int key0 = j * kBlockN;
+                const int key0 = ((two ? item_field(offsetof(WorkItem, kv_begin)) : 0) + j) * kBlockN;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -677,12 +761,126 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
         // ---- epilogue ---------------------------------------------------------
         if (ok) ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarOFull + t), 0, abort_flag, timeout, kSiteSoftO));
-        if (ok) {
+        // The last QK MMA of this tile has completed, so its Q tile is free: final values are
+        // staged there in the 128-byte swizzled layout the store map expects.
+        const uint32_t stage = sq + static_cast<uint32_t>(t * C::kTileBytes);
+        auto stage32 = [&](int c, const float (&v)[32]) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+            const int sub = (c * 32) / 64;
+            const int chunk0 = ((c * 32) % 64) / 8;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int phys = (chunk0 + q) ^ (r & 7);
+                const uint32_t addr = stage + static_cast<uint32_t>(sub * kSubBytes + r * 128 + phys * 16);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+                             :: "r"(addr), "r"(packed[4 * q]), "r"(packed[4 * q + 1]),
+                                "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3]) : "memory");
+            }
+        };
+        auto store_tile = [&]() {
+            fence_proxy_async_smem();
+            mbar_arrive(bar(C::kBarEpi + t));
+            if (r == 0) {
+                if (wait_bounded(bar(C::kBarEpi + t), 0, abort_flag, timeout, kSiteEpilogue)) {
+#pragma unroll
+                    for (int s = 0; s < C::kSub; ++s)
+                        tma_store_3d(&tm_o, stage + static_cast<uint32_t>(s * kSubBytes), s * 64,
+                                     q_row0 + t * kBlockM, slab);
+                    tma_store_commit();
+                    tma_store_wait_read_all();
+                }
+            }
+        };
+        const int e_nchunks = two ? item_field(offsetof(WorkItem, nchunks)) : 1;
+        if (two && e_nchunks > 1) {
+            const int nchunks = e_nchunks;
+            const int chunk = item_field(offsetof(WorkItem, chunk));
+            const int e_slab = item_field(offsetof(WorkItem, slab_local));
+            const long long unit_slot = static_cast<long long>(e_slab) * p.items + item_field(offsetof(WorkItem, item_first));
+            const long long counter = static_cast<long long>(e_slab) * p.num_units + item_field(offsetof(WorkItem, unit));
+            // ---- a chunk of a split unit: write this row's partial (O on this chunk's base,
+            // the raw row max, the row sum), count the chunk in; the chunk that completes the
+            // unit merges every chunk's partial in chunk order (so the result does not depend
+            // on which chunk finishes last) and stores the output. Nothing waits on another CTA.
+            constexpr int kTilesPerCta = two ? kQTiles : 1;
+            const size_t chunk_stride = static_cast<size_t>(kTilesPerCta) * C::kPartTileFloats;
+            // This tile's partial in chunk 0 of the unit; chunk cc is chunk_stride floats further.
+            float* unit_tile = p.partial + static_cast<size_t>(unit_slot) * chunk_stride +
+                               static_cast<size_t>(t) * C::kPartTileFloats;
+            if (ok) {
+                tc_fence_after();
+                float* mine = unit_tile + static_cast<size_t>(chunk) * chunk_stride;
+                float4* cols = reinterpret_cast<float4*>(mine);
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
+                    tmem_wait_ld();
+                    reg_fence32(o);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        cols[(c * 8 + q) * kBlockM + r] =
+                            make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
+                                        __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
+                }
+                mine[D * kBlockM + r] = row_max;
+                mine[D * kBlockM + kBlockM + r] = row_sum;
+                __threadfence();
+                mbar_arrive(bar(C::kBarPart));
+            }
+            if (threadIdx.x == 0) {
+                uint32_t flag = 2u;     // gave up
+                if (ok && wait_bounded(bar(C::kBarPart), 0, abort_flag, timeout, kSitePartial)) {
+                    const unsigned int done = atomicAdd(p.counters + counter, 1u);
+                    flag = done == static_cast<unsigned int>(nchunks - 1) ? 1u : 0u;
+                }
+                *last_flag = flag;
+                mbar_arrive(bar(C::kBarPartDone));
+            }
+            if (ok) ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarPartDone), 0, abort_flag, timeout, kSitePartial));
+            if (ok && *last_flag == 1u) {
+                __threadfence();
+                float top = -INFINITY;
+                for (int cc = 0; cc < nchunks; ++cc)
+                    top = fmaxf(top, __ldcg(unit_tile + cc * chunk_stride + D * kBlockM + r));
+                const float top_base = exp_base(top, sl2);
+                auto weight = [&](float m) { return m == -INFINITY ? 0.0f : ex2_approx(exp_base(m, sl2) - top_base); };
+                float total = 0.0f;
+                for (int cc = 0; cc < nchunks; ++cc) {
+                    const float* tc = unit_tile + cc * chunk_stride;
+                    total = __fadd_rn(total, __fmul_rn(weight(__ldcg(tc + D * kBlockM + r)),
+                                                       __ldcg(tc + D * kBlockM + kBlockM + r)));
+                }
+                const float inv = total > 0.0f ? 1.0f / total : 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    float acc[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+                    for (int cc = 0; cc < nchunks; ++cc) {
+                        const float* tc = unit_tile + cc * chunk_stride;
+                        const float w = weight(__ldcg(tc + D * kBlockM + r));
+                        const float4* cols = reinterpret_cast<const float4*>(tc);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 x = __ldcg(cols + (c * 8 + q) * kBlockM + r);
+                            acc[4 * q] = fmaf(w, x.x, acc[4 * q]);
+                            acc[4 * q + 1] = fmaf(w, x.y, acc[4 * q + 1]);
+                            acc[4 * q + 2] = fmaf(w, x.z, acc[4 * q + 2]);
+                            acc[4 * q + 3] = fmaf(w, x.w, acc[4 * q + 3]);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] *= inv;
+                    stage32(c, acc);
+                }
+                store_tile();
+            }
+        } else if (ok) {
             tc_fence_after();
             const float inv = row_sum > 0.0f ? 1.0f / row_sum : 0.0f;
-            // The last QK MMA of this tile has completed, so its Q tile is free:
-            // stage O there in the 128-byte swizzled layout the store map expects.
-            const uint32_t stage = sq + static_cast<uint32_t>(t * C::kTileBytes);
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 uint32_t o[32];
@@ -705,33 +903,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     }
                 }
 #endif
-                uint32_t packed[16];
+                float v[32];
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-                const int sub = (c * 32) / 64;
-                const int chunk0 = ((c * 32) % 64) / 8;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int phys = (chunk0 + q) ^ (r & 7);
-                    const uint32_t addr = stage + static_cast<uint32_t>(sub * kSubBytes + r * 128 + phys * 16);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
-                                 :: "r"(addr), "r"(packed[4 * q]), "r"(packed[4 * q + 1]),
-                                    "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3]) : "memory");
-                }
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
+                stage32(c, v);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(bar(C::kBarEpi + t));
-            if (r == 0) {
-                if (wait_bounded(bar(C::kBarEpi + t), 0, abort_flag, timeout, kSiteEpilogue)) {
-#pragma unroll
-                    for (int s = 0; s < C::kSub; ++s)
-                        tma_store_3d(&tm_o, stage + static_cast<uint32_t>(s * kSubBytes), s * 64,
-                                     q_row0 + t * kBlockM, slab);
-                    tma_store_commit();
-                    tma_store_wait_read_all();
-                }
-            }
+            store_tile();
         }
         tc_fence_before();
     } else {
@@ -912,7 +1089,7 @@ template <int D>
 int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
            const Params& params, bool one_tile, long long slabs, cudaStream_t stream)
 {
-    const long long blocks = slabs * params.num_units;
+    const long long blocks = slabs * params.items;
     if (blocks <= 0) return FA_STATUS_OK;
     if (blocks > INT_MAX) return FA_STATUS_INVALID_ARGUMENT;
     const unsigned grid = static_cast<unsigned>(blocks);
@@ -929,6 +1106,52 @@ thread_local unsigned long long t_armed_stall_ns = 0;
 // Test-only: the kernel instantiation for this host thread's launches (fa_sm100_test_force_kernel):
 // 0 = the launcher's choice, 1 = one Q tile per CTA, 2 = row pairs.
 thread_local int t_forced_kernel = 0;
+// Test-only: the causal key-range split for this host thread's launches
+// (fa_sm100_test_force_split): -1 = the launcher's choice, 0 = none, L > 0 = chunks of L key tiles.
+thread_local int t_forced_split = -1;
+
+// Workspace of split launches (partials and per-unit counters): stream-ordered allocations from
+// a per-device pool (cudaMallocFromPoolAsync / cudaFreeAsync on the launch stream), so that
+// concurrent launches on different streams never share a workspace; the pool keeps its memory
+// between launches (release threshold at its maximum).
+struct SplitPool {
+    std::once_flag once;
+    int status = FA_STATUS_OK;
+    cudaMemPool_t pool = nullptr;
+};
+SplitPool g_split_pools[kMaxDevices];
+
+int split_pool(int device, cudaMemPool_t* out)
+{
+    SplitPool& sp = g_split_pools[device];
+    std::call_once(sp.once, [&]() {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        cudaError_t err = cudaMemPoolCreate(&sp.pool, &props);
+        if (err == cudaSuccess) {
+            uint64_t keep = UINT64_MAX;
+            err = cudaMemPoolSetAttribute(sp.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        if (err != cudaSuccess) {
+            sp.status = static_cast<int>(err);
+            cudaGetLastError();
+        }
+    });
+    *out = sp.pool;
+    return sp.status;
+}
+
+// Key tiles of unit u (a row pair) of a causal launch, and the chunks of a split.
+inline int pair_tiles(int u, int kv_all) { return std::min(kv_all, 2 * u + 2); }
+inline int split_items(int units, int kv_all, int split_len)
+{
+    int items = 0;
+    for (int u = 0; u < units; ++u) items += (pair_tiles(u, kv_all) + split_len - 1) / split_len;
+    return items;
+}
 
 int forward(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len, int head_dim,
             int causal, long long slab_begin, long long slab_end, void* stream, int inject_stall,
@@ -953,15 +1176,29 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
         t_armed_stall_ns = 0;
     }
     const long long count = slab_end - slab_begin;
+    const int sms = g_devices[device].sm_count;
     Params params{};
     params.seq_len = seq_len;
-    // Small-grid dispatch: a CTA normally takes a row pair (two Q tiles whose softmax phases
-    // overlap on one SM). When even one CTA per Q tile would leave SMs idle, each Q tile gets
-    // its own CTA instead: twice the CTAs, each with a shorter critical path.
+    // Kernel choice. A CTA normally takes a row pair (two Q tiles whose softmax phases overlap
+    // on one SM). Dense: when even one CTA per Q tile would leave SMs idle, each Q tile gets its
+    // own CTA instead (twice the CTAs, each with a shorter critical path). Causal: when the row
+    // pairs fit in one wave, the longest CTA sets the time, and one Q tile per CTA shortens it
+    // (measured on B200: 0.82-0.87x the row-pair time at (1,8,4096,D) and (2,8,2048,D)).
     const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
-    bool single = count * pairs * kQTiles <= g_devices[device].sm_count;
+    const int kv_all = (seq_len + kBlockN - 1) / kBlockN;
+    bool single = causal ? count * pairs <= sms : count * pairs * kQTiles <= sms;
     if (t_forced_kernel != 0) single = t_forced_kernel == 1;
     params.num_units = single ? (seq_len + kBlockM - 1) / kBlockM : pairs;
+    // Causal key-range split (row-pair kernel only): chunks of split_len key tiles.
+    int split_len = 0;
+    if (t_forced_split >= 0) split_len = t_forced_split;
+    if (single || !causal) split_len = 0;
+    if (split_len > 0) {
+        split_len = std::max(split_len, (kv_all + kMaxChunks - 1) / kMaxChunks);
+        if (split_len >= kv_all) split_len = 0;         // no unit would be split
+    }
+    params.split_len = split_len;
+    params.items = split_len > 0 ? split_items(pairs, kv_all, split_len) : params.num_units;
     params.slab_begin = slab_begin;
     params.scale_log2 = fa_default_scale(head_dim) * 1.4426950408889634f;
     params.causal = causal ? 1 : 0;
@@ -975,8 +1212,36 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
         const long long by_l2 = kv_bytes > 0 ? (32LL << 20) / kv_bytes : count;
         params.chunk = static_cast<int>(std::max(1LL, std::min(count, by_l2)));
     }
-    return head_dim == 64 ? launch<64>(maps->q, maps->k, maps->v, maps->o, params, single, count, s)
-                          : launch<128>(maps->q, maps->k, maps->v, maps->o, params, single, count, s);
+    void* workspace = nullptr;
+    if (split_len > 0) {
+        // [counters: slabs * units u32, padded to 256 B][partials: slabs * items * 2 tiles *
+        // (D + 2) * 128 floats]
+        const size_t counter_bytes = ((static_cast<size_t>(count) * pairs * 4u) + 255u) & ~static_cast<size_t>(255u);
+        const size_t partial_bytes = static_cast<size_t>(count) * params.items * kQTiles *
+                                     static_cast<size_t>(head_dim + 2) * kBlockM * sizeof(float);
+        cudaMemPool_t pool = nullptr;
+        int pool_status = split_pool(device, &pool);
+        if (pool_status == FA_STATUS_OK &&
+            cudaMallocFromPoolAsync(&workspace, counter_bytes + partial_bytes, pool, s) == cudaSuccess &&
+            cudaMemsetAsync(workspace, 0, counter_bytes, s) == cudaSuccess) {
+            params.counters = static_cast<unsigned int*>(workspace);
+            params.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes);
+        } else {
+            // No workspace: the unsplit launch computes the same result.
+            cudaGetLastError();
+            if (workspace != nullptr) cudaFreeAsync(workspace, s);
+            workspace = nullptr;
+            params.split_len = 0;
+            params.items = params.num_units;
+        }
+    }
+    const int launched = head_dim == 64 ? launch<64>(maps->q, maps->k, maps->v, maps->o, params, single, count, s)
+                                        : launch<128>(maps->q, maps->k, maps->v, maps->o, params, single, count, s);
+    if (workspace != nullptr) {
+        const cudaError_t freed = cudaFreeAsync(workspace, s);
+        if (launched == FA_STATUS_OK && freed != cudaSuccess) return static_cast<int>(freed);
+    }
+    return launched;
 }
 
 }  // namespace
@@ -1029,6 +1294,13 @@ int fa_sm100_test_arm_stall(unsigned long long timeout_ns)
 {
     if (timeout_ns == 0 || timeout_ns > kDefaultTimeoutNs) return FA_STATUS_INVALID_ARGUMENT;
     t_armed_stall_ns = timeout_ns;
+    return FA_STATUS_OK;
+}
+
+int fa_sm100_test_force_split(int split_len)
+{
+    if (split_len < -1) return FA_STATUS_INVALID_ARGUMENT;
+    t_forced_split = split_len;
     return FA_STATUS_OK;
 }
 

@@ -153,6 +153,13 @@ FA_API int fa_sm100_test_arm_stall(unsigned long long timeout_ns);
  * until changed. No reference counterpart. */
 FA_API int fa_sm100_test_force_kernel(int kind);
 
+/* Test-only: the causal key-range split for this host thread's launches of the row-pair
+ * kernel -- -1 the launcher's own choice (the default), 0 never, L > 0 every row pair with
+ * more than L key tiles is processed by several CTAs of at most L key tiles each, whose
+ * partial results the last of them merges (L is raised where a pair would need more than
+ * 64 chunks). Stays set until changed. No reference counterpart. */
+FA_API int fa_sm100_test_force_split(int split_len);
+
 /* End-to-end call with HOST buffers (pageable or pinned): copies Q/K/V in,
  * runs the forward pass and copies O out, pipelined over slab chunks on two
  * streams of the current device, then synchronises. Uses staging buffers that

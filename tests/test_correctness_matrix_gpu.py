@@ -7,8 +7,8 @@ against the CPU FP64 oracle with the gate "no non-finite output and max row-scal
 <= 2.0". That is 280 cases; each runs here twice:
 
 * as (1, 2, N, D), which the launcher gives one 128-row Q tile per CTA (small grid), and
-* as the same two slabs repeated 38 times, (38, 2, N, D) = 76 slabs, large enough for the
-  row-pair CTAs; every slab must then match its oracle slab.
+* as the same two slabs repeated 38 times, (38, 2, N, D) = 76 slabs, with the row-pair kernel
+  forced (fa_sm100_test_force_kernel); every slab must then match its oracle slab.
 
 Outputs are NaN-poisoned before each launch (stronger than the reference's zero fill).
 """
@@ -36,7 +36,8 @@ def _run(dq, dk, dv, shape, causal):
 @pytest.mark.parametrize("causal", [0, 1])
 def test_reference_correctness_matrix(oracle, cuda_device, d, causal):
     import torch
-    from cuda_fused_attention_b200 import AttentionShape, device_status
+    from cuda_fused_attention_b200 import AttentionShape, device_status, _lib
+    lib = _lib.load()
     worst = {}
     for n in LENGTHS:
         for family in range(5):
@@ -48,7 +49,11 @@ def test_reference_correctness_matrix(oracle, cuda_device, d, causal):
             assert acc["output_nan"] == 0 and acc["output_inf"] == 0, ("one tile", n, family, acc)
             assert acc["passed"], ("one tile", n, family, acc)
             tiled = [t.repeat(REPEAT) for t in dev]
-            got_pairs = _run(*tiled, AttentionShape(REPEAT, 2, n, d), causal)
+            assert lib.fa_sm100_test_force_kernel(2) == 0
+            try:
+                got_pairs = _run(*tiled, AttentionShape(REPEAT, 2, n, d), causal)
+            finally:
+                lib.fa_sm100_test_force_kernel(0)
             acc_pairs = oracle.compare(got_pairs, np.tile(ref, REPEAT), d, TOL)
             assert acc_pairs["output_nan"] == 0 and acc_pairs["output_inf"] == 0, ("row pairs", n, family)
             assert acc_pairs["passed"], ("row pairs", n, family, acc_pairs)

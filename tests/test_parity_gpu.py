@@ -89,12 +89,14 @@ def test_boundary_lengths(oracle, cuda_device, d, causal):
         _full_case(oracle, cuda_device, 1, 2, n, d, causal)
 
 
-def _single_tile_dispatch(slabs, n):
+def _single_tile_dispatch(slabs, n, causal=False):
     """The launcher's small-grid rule: one 128-row Q tile per CTA when a CTA per Q tile would
-    still leave SMs idle (slabs * row pairs * 2 <= SM count), else a row pair per CTA."""
+    still leave SMs idle (dense: slabs * row pairs * 2 <= SM count), or when the row pairs fit
+    in one wave (causal: slabs * row pairs <= SM count); else a row pair per CTA."""
     import torch
     sm_count = torch.cuda.get_device_properties(0).multi_processor_count
-    return slabs * ((n + 255) // 256) * 2 <= sm_count
+    pairs = slabs * ((n + 255) // 256)
+    return (pairs if causal else pairs * 2) <= sm_count
 
 
 @pytest.mark.parametrize("d", [64, 128])
@@ -103,11 +105,17 @@ def test_boundary_lengths_row_pairs(oracle, cuda_device, d, causal):
     """The same boundaries on a grid large enough for row-pair CTAs, including pairs whose
     second Q tile has no valid row (N = 128, 257, 300, 383, 513): that tile is computed on
     zero-filled rows and its store is clipped."""
+    from cuda_fused_attention_b200 import _lib
+    lib = _lib.load()
     b, h = 3, 25
-    for n in (1, 65, 128, 129, 255, 256, 257, 300, 383, 513):
-        assert not _single_tile_dispatch(b * h, n)
-        _full_case(oracle, cuda_device, b, h, n, d, causal)
-    assert _single_tile_dispatch(2, 513)       # the (1, 2, N) cases above ran one tile per CTA
+    try:
+        assert lib.fa_sm100_test_force_kernel(2) == 0      # row pairs, whatever the grid
+        for n in (1, 65, 128, 129, 255, 256, 257, 300, 383, 513):
+            _full_case(oracle, cuda_device, b, h, n, d, causal)
+    finally:
+        lib.fa_sm100_test_force_kernel(0)
+    assert not _single_tile_dispatch(b * h, 513, causal)
+    assert _single_tile_dispatch(2, 513, causal)   # the (1, 2, N) cases above ran one tile per CTA
     check_device_clean()
 
 
