@@ -46,6 +46,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -118,7 +119,7 @@ struct Cfg {
     static constexpr int kBarDrain = kBarEpi + 2;
     static constexpr int kBarNever = kBarDrain + 1;
     static constexpr int kBarPart = kBarNever + 1;        // split: all softmax threads wrote their partial rows
-    static constexpr int kBarPartDone = kBarPart + 1;     // split: this chunk has been counted in
+    static constexpr int kBarPartDone = kBarPart + 1;     // split: this chunk has counted itself in
     static constexpr int kNumBars = kBarPartDone + 1;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;   // tmem base, abort flag, last-chunk flag (u32)
     static constexpr int kItemOff = kMiscOff + 16;            // the CTA's work item (WorkItem), for the epilogue
@@ -141,10 +142,11 @@ struct WorkItem {
     int unit;           // row pair (or Q tile in the one-tile kernel) of the slab
     int chunk;          // chunk of the unit's key range
     int nchunks;        // chunks the unit's key range is split into (1 = not split)
-    int item_first;     // work item of the unit's chunk 0 (indexes the partials)
+    int reserved0;      // (unused: with the key-tile range at this offset ptxas allocates the
+                        //  row-pair kernel without a spill)
     int kv_begin;       // first key tile of this CTA
     int n_kv;           // key tiles of this CTA
-    int pad;
+    int reserved1;
 };
 
 struct Params {
@@ -159,11 +161,14 @@ struct Params {
     int chunk;                  // causal block order: slabs per group (see the kernel's work item)
     // Causal key-range split (0 = none): a unit with more than split_len key tiles is processed
     // by ceil(tiles / split_len) CTAs ("chunks"), each over a contiguous range of its key tiles;
-    // every chunk writes an unnormalised partial and the last to finish merges them.
+    // the last chunk of a unit to finish merges the others' partials into the output.
     int split_len;
     int items;                  // work items per slab: units, or chunks when split
-    float* partial;             // [slabs * items][Q tiles][Cfg::kPartTileFloats] (split only)
-    unsigned int* counters;     // [slabs * num_units] chunks done per unit, zero at launch (split only)
+    int max_chunks;             // chunks of the heaviest unit (the stride of the per-unit arrays)
+    unsigned long long epoch;   // this launch's tag (48 bits) in the arrival counters and flags
+    unsigned long long* arrive; // [slabs * num_units]: epoch << 16 | chunks counted in
+    unsigned long long* flags;  // [slabs * num_units * max_chunks]: epoch once that chunk's partial is written
+    float* partial;             // [slabs * num_units * max_chunks][Q tiles][Cfg::kPartTileFloats]
 };
 
 // Device error word of this module instance (one per device). Bit 0: some wait
@@ -296,15 +301,18 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 }
 
 // kOneTile = false: a CTA per row pair (two Q tiles). kOneTile = true: a CTA per 128-row
-// Q tile, for grids too small to fill the GPU with pairs; warpgroup 1 then idles. Two
-// instantiations, so that the pair kernel carries no branch for the single-tile case.
-template <int D, bool kOneTile>
+// Q tile, for grids too small to fill the GPU with pairs; warpgroup 1 then idles.
+// kSplit = true (row pairs only): the causal key-range split (Params::split_len). Separate
+// instantiations, so that the row-pair kernel carries no code of the other two: the split's
+// epilogue alone, compiled into it, made its main loop 2-17 % slower.
+template <int D, bool kOneTile, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
               const Params p)
 {
     using C = Cfg<D>;
+    static_assert(!(kSplit && kOneTile), "the key-range split is a row-pair kernel feature");
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment: the 128-byte swizzle pattern repeats every 8 rows.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -349,7 +357,6 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     long long slab_local;
     int unit;
     int chunk = 0, nchunks = 1;
-    long long item_first = 0;   // split: the work item of chunk 0 of this unit
     if (p.causal) {
         const long long per_group = static_cast<long long>(p.chunk) * p.items;
         const long long group = block / per_group;
@@ -358,9 +365,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const long long within = block - group * per_group;
         const long long level = within / in_group;
         slab_local = first + (within - level * in_group);
-        if (two && p.split_len > 0) {
-            // Items of a slab: units heaviest first, each unit's chunks in key order (the split
-            // is a row-pair-kernel feature; the host never asks the one-tile kernel for it).
+        if (kSplit && p.split_len > 0) {
+            // Items of a slab: units heaviest first, each unit's chunks in key order.
             int item = static_cast<int>(level);
             unit = 0;
             for (int u = p.num_units - 1; u >= 0; --u) {
@@ -373,7 +379,6 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 }
                 item -= ncu;
             }
-            item_first = level - chunk;
         } else {
             unit = p.num_units - 1 - static_cast<int>(level);
         }
@@ -395,13 +400,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     // host splits only units with at most kMaxChunks chunks, so c * tiles < 2^31).
     const int kv_begin_0 = chunk * tiles / nchunks;
     const int n_kv_0 = (chunk + 1) * tiles / nchunks - kv_begin_0;
-    if (two && threadIdx.x == 0) {
+    if (kSplit && threadIdx.x == 0) {
         WorkItem* item_smem = reinterpret_cast<WorkItem*>(smem + C::kItemOff);
         item_smem->slab_local = static_cast<int>(slab_local);
         item_smem->unit = unit;
         item_smem->chunk = chunk;
         item_smem->nchunks = nchunks;
-        item_smem->item_first = static_cast<int>(item_first);
         item_smem->kv_begin = kv_begin_0;
         item_smem->n_kv = n_kv_0;
     }
@@ -428,8 +432,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     // Key tiles of this CTA: [kv_begin, kv_begin + n_kv) (loaded where each role starts).
-    const int kv_begin = two ? item_field(offsetof(WorkItem, kv_begin)) : 0;
-    const int n_kv = two ? item_field(offsetof(WorkItem, n_kv)) : n_kv_0;
+    const int kv_begin = kSplit ? item_field(offsetof(WorkItem, kv_begin)) : 0;
+    const int n_kv = kSplit ? item_field(offsetof(WorkItem, n_kv)) : n_kv_0;
     const unsigned long long timeout = p.timeout_ns;
 
     if (warp == kLoadWarp) {
@@ -683,7 +687,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
             const bool mask_tile = (p.causal && j >= diag_local) || j >= tail_local;
             if (mask_tile) {
-                const int key0 = ((two ? item_field(offsetof(WorkItem, kv_begin)) : 0) + j) * kBlockN;
+                const int key0 = ((kSplit ? item_field(offsetof(WorkItem, kv_begin)) : 0) + j) * kBlockN;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -793,23 +797,50 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 }
             }
         };
-        const int e_nchunks = two ? item_field(offsetof(WorkItem, nchunks)) : 1;
-        if (two && e_nchunks > 1) {
+        const int e_nchunks = kSplit ? item_field(offsetof(WorkItem, nchunks)) : 1;
+        if (kSplit && e_nchunks > 1) {
+            // ---- a chunk of a split unit. Thread 0 counts the chunk in on the unit's arrival
+            // counter (tagged with this launch's epoch, so it needs no zeroing). A chunk that is
+            // not the last writes its partial -- O on its own base, the raw row maxima and the
+            // row sums -- and publishes it with an epoch flag. The last chunk waits (bounded) for
+            // those flags -- every chunk it waits for has already counted in, so it is running and
+            // waits for nothing -- and merges all chunks in chunk order, its own O straight from
+            // tensor memory, so the result does not depend on the order of arrival.
             const int nchunks = e_nchunks;
             const int chunk = item_field(offsetof(WorkItem, chunk));
-            const int e_slab = item_field(offsetof(WorkItem, slab_local));
-            const long long unit_slot = static_cast<long long>(e_slab) * p.items + item_field(offsetof(WorkItem, item_first));
-            const long long counter = static_cast<long long>(e_slab) * p.num_units + item_field(offsetof(WorkItem, unit));
-            // ---- a chunk of a split unit: write this row's partial (O on this chunk's base,
-            // the raw row max, the row sum), count the chunk in; the chunk that completes the
-            // unit merges every chunk's partial in chunk order (so the result does not depend
-            // on which chunk finishes last) and stores the output. Nothing waits on another CTA.
+            const long long unit_index = static_cast<long long>(item_field(offsetof(WorkItem, slab_local))) *
+                                         p.num_units + item_field(offsetof(WorkItem, unit));
             constexpr int kTilesPerCta = two ? kQTiles : 1;
             const size_t chunk_stride = static_cast<size_t>(kTilesPerCta) * C::kPartTileFloats;
             // This tile's partial in chunk 0 of the unit; chunk cc is chunk_stride floats further.
-            float* unit_tile = p.partial + static_cast<size_t>(unit_slot) * chunk_stride +
+            float* unit_tile = p.partial + static_cast<size_t>(unit_index) * p.max_chunks * chunk_stride +
                                static_cast<size_t>(t) * C::kPartTileFloats;
-            if (ok) {
+            unsigned long long* unit_flags = p.flags + unit_index * p.max_chunks;
+            if (threadIdx.x == 0) {
+                uint32_t role = 2u;     // gave up
+                if (ok) {
+                    unsigned long long* counter = p.arrive + unit_index;
+                    unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(counter);
+                    unsigned int arrival = 0;
+                    for (int attempt = 0; attempt < 1024; ++attempt) {
+                        const bool current = (seen >> 16) == p.epoch;
+                        const unsigned long long next = current ? seen + 1 : ((p.epoch << 16) | 1ull);
+                        const unsigned long long prev = atomicCAS(counter, seen, next);
+                        if (prev == seen) {
+                            arrival = current ? static_cast<unsigned int>(seen & 0xFFFFu) : 0u;
+                            role = arrival == static_cast<unsigned int>(nchunks - 1) ? 1u : 0u;
+                            break;
+                        }
+                        seen = prev;
+                    }
+                    if (role == 2u) record_timeout(abort_flag, kSitePartial);
+                }
+                *last_flag = role;
+                mbar_arrive(bar(C::kBarPartDone));
+            }
+            if (ok) ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarPartDone), 0, abort_flag, timeout, kSitePartial));
+            const uint32_t role = ok ? *last_flag : 2u;
+            if (role == 0u) {
                 tc_fence_after();
                 float* mine = unit_tile + static_cast<size_t>(chunk) * chunk_stride;
                 float4* cols = reinterpret_cast<float4*>(mine);
@@ -829,30 +860,40 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 mine[D * kBlockM + kBlockM + r] = row_sum;
                 __threadfence();
                 mbar_arrive(bar(C::kBarPart));
-            }
-            if (threadIdx.x == 0) {
-                uint32_t flag = 2u;     // gave up
-                if (ok && wait_bounded(bar(C::kBarPart), 0, abort_flag, timeout, kSitePartial)) {
-                    const unsigned int done = atomicAdd(p.counters + counter, 1u);
-                    flag = done == static_cast<unsigned int>(nchunks - 1) ? 1u : 0u;
+                if (threadIdx.x == 0 && wait_bounded(bar(C::kBarPart), 0, abort_flag, timeout, kSitePartial)) {
+                    __threadfence();
+                    st_release_gpu(unit_flags + chunk, p.epoch);
                 }
-                *last_flag = flag;
-                mbar_arrive(bar(C::kBarPartDone));
+            } else if (role == 1u) {
+                // Wait until every other chunk's partial is published (each thread polls; bounded).
+                bool ready = true;
+                for (int cc = 0; cc < nchunks && ready; ++cc) {
+                    if (cc == chunk) continue;
+                    if (ld_acquire_gpu(unit_flags + cc) == p.epoch) continue;
+                    const uint64_t begin = global_timer_ns();
+                    while (ld_acquire_gpu(unit_flags + cc) != p.epoch) {
+                        if (*abort_flag) { ready = false; break; }
+                        if (global_timer_ns() - begin > timeout) {
+                            record_timeout(abort_flag, kSitePartial);
+                            ready = false;
+                            break;
+                        }
+                    }
+                }
+                ok = __all_sync(0xffffffffu, ready);
             }
-            if (ok) ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarPartDone), 0, abort_flag, timeout, kSitePartial));
-            if (ok && *last_flag == 1u) {
-                __threadfence();
+            if (role == 1u && ok) {
+                tc_fence_after();
+                auto chunk_max = [&](int cc) { return cc == chunk ? row_max : __ldcg(unit_tile + cc * chunk_stride + D * kBlockM + r); };
+                auto chunk_sum = [&](int cc) {
+                    return cc == chunk ? row_sum : __ldcg(unit_tile + cc * chunk_stride + D * kBlockM + kBlockM + r);
+                };
                 float top = -INFINITY;
-                for (int cc = 0; cc < nchunks; ++cc)
-                    top = fmaxf(top, __ldcg(unit_tile + cc * chunk_stride + D * kBlockM + r));
+                for (int cc = 0; cc < nchunks; ++cc) top = fmaxf(top, chunk_max(cc));
                 const float top_base = exp_base(top, sl2);
                 auto weight = [&](float m) { return m == -INFINITY ? 0.0f : ex2_approx(exp_base(m, sl2) - top_base); };
                 float total = 0.0f;
-                for (int cc = 0; cc < nchunks; ++cc) {
-                    const float* tc = unit_tile + cc * chunk_stride;
-                    total = __fadd_rn(total, __fmul_rn(weight(__ldcg(tc + D * kBlockM + r)),
-                                                       __ldcg(tc + D * kBlockM + kBlockM + r)));
-                }
+                for (int cc = 0; cc < nchunks; ++cc) total = __fadd_rn(total, __fmul_rn(weight(chunk_max(cc)), chunk_sum(cc)));
                 const float inv = total > 0.0f ? 1.0f / total : 0.0f;
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
@@ -860,16 +901,24 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 #pragma unroll
                     for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
                     for (int cc = 0; cc < nchunks; ++cc) {
-                        const float* tc = unit_tile + cc * chunk_stride;
-                        const float w = weight(__ldcg(tc + D * kBlockM + r));
-                        const float4* cols = reinterpret_cast<const float4*>(tc);
+                        const float w = weight(chunk_max(cc));
+                        if (cc == chunk) {
+                            uint32_t o[32];
+                            tmem_ld32(t_o + static_cast<uint32_t>(c * 32), o);
+                            tmem_wait_ld();
+                            reg_fence32(o);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const float4 x = __ldcg(cols + (c * 8 + q) * kBlockM + r);
-                            acc[4 * q] = fmaf(w, x.x, acc[4 * q]);
-                            acc[4 * q + 1] = fmaf(w, x.y, acc[4 * q + 1]);
-                            acc[4 * q + 2] = fmaf(w, x.z, acc[4 * q + 2]);
-                            acc[4 * q + 3] = fmaf(w, x.w, acc[4 * q + 3]);
+                            for (int i = 0; i < 32; ++i) acc[i] = fmaf(w, __uint_as_float(o[i]), acc[i]);
+                        } else {
+                            const float4* cols = reinterpret_cast<const float4*>(unit_tile + cc * chunk_stride);
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const float4 v4 = __ldcg(cols + (c * 8 + q) * kBlockM + r);
+                                acc[4 * q] = fmaf(w, v4.x, acc[4 * q]);
+                                acc[4 * q + 1] = fmaf(w, v4.y, acc[4 * q + 1]);
+                                acc[4 * q + 2] = fmaf(w, v4.z, acc[4 * q + 2]);
+                                acc[4 * q + 3] = fmaf(w, v4.w, acc[4 * q + 3]);
+                            }
                         }
                     }
 #pragma unroll
@@ -973,24 +1022,20 @@ int prepare_device(int device)
         if (major != 10) { state.status = FA_STATUS_NO_SM100; return; }
         err = cudaDeviceGetAttribute(&state.sm_count, cudaDevAttrMultiProcessorCount, device);
         if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
-        err = cudaFuncSetAttribute(fa_fwd_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   Cfg<64>::kSmemBytes);
-        if (err == cudaSuccess)
-            err = cudaFuncSetAttribute(fa_fwd_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg<64>::kSmemBytes);
-        if (err == cudaSuccess)
-            err = cudaFuncSetAttribute(fa_fwd_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg<128>::kSmemBytes);
-        if (err == cudaSuccess)
-            err = cudaFuncSetAttribute(fa_fwd_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg<128>::kSmemBytes);
+        const void* const kernels[] = {
+            reinterpret_cast<const void*>(fa_fwd_kernel<64, false, false>),
+            reinterpret_cast<const void*>(fa_fwd_kernel<64, true, false>),
+            reinterpret_cast<const void*>(fa_fwd_kernel<64, false, true>),
+            reinterpret_cast<const void*>(fa_fwd_kernel<128, false, false>),
+            reinterpret_cast<const void*>(fa_fwd_kernel<128, true, false>),
+            reinterpret_cast<const void*>(fa_fwd_kernel<128, false, true>)};
+        for (int i = 0; i < 6 && err == cudaSuccess; ++i)
+            err = cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       i < 3 ? Cfg<64>::kSmemBytes : Cfg<128>::kSmemBytes);
         if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
         // The warpgroup register split (setmaxnreg) waits forever if the CTA launched with
         // fewer registers than it hands out: refuse to launch such a build.
-        for (const void* func : {reinterpret_cast<const void*>(fa_fwd_kernel<64, false>),
-                                 reinterpret_cast<const void*>(fa_fwd_kernel<64, true>),
-                                 reinterpret_cast<const void*>(fa_fwd_kernel<128, false>),
-                                 reinterpret_cast<const void*>(fa_fwd_kernel<128, true>)}) {
+        for (const void* func : kernels) {
             cudaFuncAttributes attributes{};
             err = cudaFuncGetAttributes(&attributes, func);
             if (err != cudaSuccess) { state.status = static_cast<int>(err); return; }
@@ -1089,14 +1134,17 @@ template <int D>
 int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
            const Params& params, bool one_tile, long long slabs, cudaStream_t stream)
 {
+    const bool split = !one_tile && params.split_len > 0;
     const long long blocks = slabs * params.items;
     if (blocks <= 0) return FA_STATUS_OK;
     if (blocks > INT_MAX) return FA_STATUS_INVALID_ARGUMENT;
     const unsigned grid = static_cast<unsigned>(blocks);
     if (one_tile)
-        fa_fwd_kernel<D, true><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+        fa_fwd_kernel<D, true, false><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+    else if (split)
+        fa_fwd_kernel<D, false, true><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
     else
-        fa_fwd_kernel<D, false><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
+        fa_fwd_kernel<D, false, false><<<grid, kThreads, Cfg<D>::kSmemBytes, stream>>>(mq, mk, mv, mo, params);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -1110,7 +1158,7 @@ thread_local int t_forced_kernel = 0;
 // (fa_sm100_test_force_split): -1 = the launcher's choice, 0 = none, L > 0 = chunks of L key tiles.
 thread_local int t_forced_split = -1;
 
-// Workspace of split launches (partials and per-unit counters): stream-ordered allocations from
+// Workspace of split launches (arrival counters, flags, partials): stream-ordered allocations from
 // a per-device pool (cudaMallocFromPoolAsync / cudaFreeAsync on the launch stream), so that
 // concurrent launches on different streams never share a workspace; the pool keeps its memory
 // between launches (release threshold at its maximum).
@@ -1214,18 +1262,26 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     }
     void* workspace = nullptr;
     if (split_len > 0) {
-        // [counters: slabs * units u32, padded to 256 B][partials: slabs * items * 2 tiles *
-        // (D + 2) * 128 floats]
-        const size_t counter_bytes = ((static_cast<size_t>(count) * pairs * 4u) + 255u) & ~static_cast<size_t>(255u);
-        const size_t partial_bytes = static_cast<size_t>(count) * params.items * kQTiles *
-                                     static_cast<size_t>(head_dim + 2) * kBlockM * sizeof(float);
+        // [arrival counters: slabs * units u64][flags: slabs * units * max_chunks u64]
+        // [partials: slabs * units * max_chunks * 2 tiles * (D + 2) * 128 floats]. Nothing needs
+        // zeroing: counters and flags carry this launch's epoch.
+        params.max_chunks = (kv_all + split_len - 1) / split_len;
+        const size_t units = static_cast<size_t>(count) * pairs;
+        const size_t arrive_bytes = units * 8u;
+        const size_t flag_bytes = units * params.max_chunks * 8u;
+        const size_t partial_bytes = units * params.max_chunks * kQTiles * static_cast<size_t>(head_dim + 2) * kBlockM *
+                                     sizeof(float);
         cudaMemPool_t pool = nullptr;
         int pool_status = split_pool(device, &pool);
         if (pool_status == FA_STATUS_OK &&
-            cudaMallocFromPoolAsync(&workspace, counter_bytes + partial_bytes, pool, s) == cudaSuccess &&
-            cudaMemsetAsync(workspace, 0, counter_bytes, s) == cudaSuccess) {
-            params.counters = static_cast<unsigned int*>(workspace);
-            params.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes);
+            cudaMallocFromPoolAsync(&workspace, arrive_bytes + flag_bytes + partial_bytes, pool, s) == cudaSuccess) {
+            static std::atomic<unsigned long long> epochs{0};
+            unsigned long long epoch = 0;
+            while (epoch == 0) epoch = (epochs.fetch_add(1) + 1) & ((1ull << 48) - 1);
+            params.epoch = epoch;
+            params.arrive = static_cast<unsigned long long*>(workspace);
+            params.flags = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + arrive_bytes);
+            params.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + arrive_bytes + flag_bytes);
         } else {
             // No workspace: the unsplit launch computes the same result.
             cudaGetLastError();
@@ -1354,8 +1410,8 @@ int fa_sm100_query(int head_dim, FaTilingInfo* info)
     if (err != cudaSuccess) return static_cast<int>(err);
     const int status = prepare_device(device);
     if (status != FA_STATUS_OK) return status;
-    const void* func = head_dim == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<64, false>)
-                                      : reinterpret_cast<const void*>(fa_fwd_kernel<128, false>);
+    const void* func = head_dim == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<64, false, false>)
+                                      : reinterpret_cast<const void*>(fa_fwd_kernel<128, false, false>);
     const int dynamic_bytes = head_dim == 64 ? Cfg<64>::kSmemBytes : Cfg<128>::kSmemBytes;
     cudaFuncAttributes attributes{};
     if ((err = cudaFuncGetAttributes(&attributes, func)) != cudaSuccess) return static_cast<int>(err);

@@ -105,6 +105,19 @@ __device__ __forceinline__ void tma_store_wait_read_all()
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// 64-bit loads/stores with GPU-scope acquire/release semantics (flags between CTAs).
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* ptr)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(unsigned long long* ptr, unsigned long long v)
+{
+    asm volatile("st.release.gpu.global.b64 [%0], %1;" :: "l"(ptr), "l"(v) : "memory");
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA store).
 __device__ __forceinline__ void fence_proxy_async_smem()
 {
