@@ -1203,7 +1203,7 @@ inline int split_items(int units, int kv_all, int split_len)
 
 int forward(const void* q, const void* k, const void* v, void* o, int batch, int heads, int seq_len, int head_dim,
             int causal, long long slab_begin, long long slab_end, void* stream, int inject_stall,
-            unsigned long long timeout_ns)
+            unsigned long long timeout_ns, bool allow_workspace = true)
 {
     int status = validate(q, k, v, o, batch, heads, seq_len, head_dim, slab_begin, slab_end);
     if (status != FA_STATUS_OK) return status;
@@ -1235,16 +1235,27 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
     const int kv_all = (seq_len + kBlockN - 1) / kBlockN;
     bool single = causal ? count * pairs <= sms : count * pairs * kQTiles <= sms;
-    if (t_forced_kernel != 0) single = t_forced_kernel == 1;
-    params.num_units = single ? (seq_len + kBlockM - 1) / kBlockM : pairs;
-    // Causal key-range split (row-pair kernel only): chunks of split_len key tiles.
+    // Causal key-range split (row-pair kernel only): chunks of split_len key tiles. A one-wave
+    // causal grid lasts as long as its heaviest row pair; splitting the heavy pairs' key ranges
+    // pays for its partials and merges where the grid is small (at most half a wave of pairs) or
+    // the rows are long (64 key tiles or more). Measured on B200 (CUDA-graph replay) against one
+    // Q tile per CTA: (1,8,2048,64) 26.6 -> 23.2 us in chunks of a third of the key tiles;
+    // (1,4,8192,128) 108.2 -> 87.2 us, (1,2,16384,128) 211.5 -> 156.2 us and (1,1,32768,128)
+    // 418.4 -> 295.5 us in halves; at (2,8,2048,D), (4,8,1024,D) and (1,16,2048,64) (a full wave
+    // of pairs with short rows) the split was slower.
     int split_len = 0;
+    if (causal && count * pairs <= sms && kv_all >= 16 && (2 * count * pairs <= sms || kv_all >= 64)) {
+        split_len = kv_all >= 64 ? (kv_all + 1) / 2 : (kv_all + 2) / 3;
+        single = false;
+    }
     if (t_forced_split >= 0) split_len = t_forced_split;
-    if (single || !causal) split_len = 0;
+    if (t_forced_kernel != 0) single = t_forced_kernel == 1;
+    if (single || !causal || !allow_workspace) split_len = 0;
     if (split_len > 0) {
         split_len = std::max(split_len, (kv_all + kMaxChunks - 1) / kMaxChunks);
         if (split_len >= kv_all) split_len = 0;         // no unit would be split
     }
+    params.num_units = single ? (seq_len + kBlockM - 1) / kBlockM : pairs;
     params.split_len = split_len;
     params.items = split_len > 0 ? split_items(pairs, kv_all, split_len) : params.num_units;
     params.slab_begin = slab_begin;
@@ -1303,6 +1314,14 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
 }  // namespace
 
 namespace fa_sm100_internal {
+
+int forward_without_workspace(const void* q, const void* k, const void* v, void* o, int batch, int heads,
+                              int seq_len, int head_dim, int causal, void* stream)
+{
+    const long long slabs = (batch > 0 && heads > 0) ? static_cast<long long>(batch) * heads : 0;
+    return forward(q, k, v, o, batch, heads, seq_len, head_dim, causal, 0, slabs, stream, 0, kDefaultTimeoutNs,
+                   false);
+}
 
 int take_error_word(cudaStream_t stream, unsigned int* word)
 {

@@ -7,6 +7,11 @@
 
 namespace fa_sm100_internal {
 
+// fa_sm100_fwd without the causal key-range split, the one launch that takes workspace memory
+// (from a stream-ordered pool): a launch that allocates nothing, for fa_sm100_fwd_host_static.
+int forward_without_workspace(const void* q, const void* k, const void* v, void* o, int batch, int heads,
+                              int seq_len, int head_dim, int causal, void* stream);
+
 // Reads the device error word of the current device on `stream` (a copy ordered
 // after the work already queued there, then a synchronisation of that stream)
 // and clears it if it was set. Returns FA_STATUS_OK or FA_STATUS_DEVICE_TIMEOUT,

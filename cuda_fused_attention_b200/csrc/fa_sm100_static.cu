@@ -20,7 +20,9 @@
 //   * No cudaMalloc, cudaFree, stream or event creation, and no allocating
 //     library routine: copies, the kernel and the synchronisation all run on
 //     the stream the caller passes (NULL = legacy default stream). The chunks
-//     run one after another on that stream (no copy/compute overlap).
+//     run one after another on that stream (no copy/compute overlap). Their
+//     launches never use the causal key-range split, whose workspace would
+//     come from a memory pool.
 //   * Set-up: the first call on a device, with that device current, resolves
 //     the array's device address once with cudaGetSymbolAddress (host code
 //     cannot use the array's name as a device address). Make that first call
@@ -127,7 +129,8 @@ int fa_sm100_fwd_host_static(const void* q_host, const void* k_host, const void*
         if ((err = cudaMemcpyAsync(dq, hq + offset, bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
         if ((err = cudaMemcpyAsync(dk, hk + offset, bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
         if ((err = cudaMemcpyAsync(dv, hv + offset, bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
-        status = fa_sm100_fwd(dq, dk, dv, dout, static_cast<int>(count), 1, seq_len, head_dim, causal, stream);
+        status = fa_sm100_internal::forward_without_workspace(dq, dk, dv, dout, static_cast<int>(count), 1, seq_len,
+                                                             head_dim, causal, stream);
         if (status != FA_STATUS_OK) break;
         if ((err = cudaMemcpyAsync(ho + offset, dout, bytes, cudaMemcpyDeviceToHost, s)) != cudaSuccess) break;
     }

@@ -63,7 +63,11 @@ typedef struct FaTilingInfo {
  * Replaces launch_attention_tensorcore_v3 (include/flash_attention.h:92,
  * kernels/v3/v3_tensorcore.cu:722-750). q, k, v, o: device pointers, 16-byte
  * aligned, each batch*heads*seq_len*head_dim bf16 elements. Every element of o
- * is written. */
+ * is written. A causal launch with few (batch, head) slabs and long rows may
+ * split the key range of its heaviest row pairs across several CTAs; such a
+ * launch takes its workspace (partials of the split rows) from a memory pool
+ * of the library, allocated and freed in order on `stream` (stream-ordered
+ * allocation, so concurrent launches on other streams never share it). */
 FA_API int fa_sm100_fwd(const void* q, const void* k, const void* v, void* o,
                  int batch, int heads, int seq_len, int head_dim, int causal, void* stream);
 

@@ -365,10 +365,12 @@ def test_one_tile_kernel_equals_row_pair_kernel(oracle, cuda_device):
     the one-tile kernel spreads a row over two threads but keeps the row-pair kernel's
     arithmetic (same base decisions, same summation order). Forced on the same shapes,
     including the x4 families, whose peaky rows move the exponent base on either half of a
-    tile; and a slab's output does not depend on how many slabs share its launch."""
+    tile. (Launches the launcher splits by key range sum in another order: within tolerance
+    of these, tests/test_split_gpu.py.)"""
     import torch
     from cuda_fused_attention_b200 import AttentionShape, _lib
     lib = _lib.load()
+    assert lib.fa_sm100_test_force_split(0) == 0      # the key-range split sums differently
     try:
         for (b, h, n, d) in [(2, 5, 1500, 64), (3, 4, 1000, 128), (1, 3, 4096, 128), (2, 2, 300, 64)]:
             for family in (0, 4, 5):
@@ -382,3 +384,4 @@ def test_one_tile_kernel_equals_row_pair_kernel(oracle, cuda_device):
         check_device_clean()
     finally:
         lib.fa_sm100_test_force_kernel(0)
+        lib.fa_sm100_test_force_split(-1)

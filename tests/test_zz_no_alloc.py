@@ -7,8 +7,11 @@ fixed file-scope __device__ array instead of cudaMalloc'd buffers. This file
 checks, through the C ABI:
 
 * calls in a row, each on different inputs than the call before (another mask
-  and input family), give the same output as the existing device entry point on
-  the same inputs, so output left in the array by an earlier call cannot pass;
+  and input family), give the output of the existing device entry point on the
+  same inputs within the tests' tolerance (the entry runs slabs in chunks, and
+  a small causal chunk may be split by key range, which sums in another order)
+  and bit-identical output when repeated, so output left in the array by an
+  earlier call cannot pass;
 * after one call at start-up (which loads the module holding the array), the
   following calls leave the device's free memory unchanged;
 * the size limit is enforced, and a device-side timeout is reported as a status
@@ -31,6 +34,10 @@ def _lib():
 
 def _ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _bf16_to_f64(bits):
+    return (bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
 
 
 def test_static_entry_rejects_oversized_slab_before_any_cuda_call():
@@ -76,13 +83,21 @@ def test_static_entry_matches_existing_entry_on_calls_in_a_row(oracle, cuda_devi
     cases = [(call, _expected(oracle, cuda_device, *call)) for call in CALLS]
     outs = [np.empty_like(want) for _, (_, want) in cases]
 
+    first = {}
+
     def static_call(i):
         (b, h, n, d, causal, _), ((q, k, v), want) = cases[i]
         got = outs[i]
         got.fill(0xFFFF)
         rc = lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None)
         assert rc == 0, (CALLS[i], rc)
-        assert np.array_equal(got, want), CALLS[i]
+        acc = oracle.compare(got, _bf16_to_f64(want), d, TOL)
+        assert acc["output_nan"] == 0 and acc["passed"], (CALLS[i], acc)
+        key = CALLS[i]
+        if key in first:
+            assert np.array_equal(got, first[key]), CALLS[i]     # a repeated call gives the same bits
+        else:
+            first[key] = got.copy()
 
     static_call(0)                       # start-up call: loads the module that holds the array
     torch.cuda.synchronize()
@@ -105,7 +120,8 @@ def test_static_entry_reports_device_timeout(oracle, cuda_device):
     (q, k, v), want = _expected(oracle, cuda_device, b, h, n, d, causal, family)
     got = np.empty_like(want)
     assert lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None) == 0
-    assert np.array_equal(got, want)     # the array's O region now holds this correct output
+    assert np.array_equal(got, want)     # the array's O region now holds this correct output (one chunk,
+                                         # the device entry's kernel)
     assert lib.fa_sm100_test_arm_stall(20_000_000) == 0
     rc = lib.fa_sm100_fwd_host_static(_ptr(q), _ptr(k), _ptr(v), _ptr(got), b, h, n, d, causal, None)
     assert rc == STATUS_DEVICE_TIMEOUT
