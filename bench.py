@@ -386,8 +386,11 @@ def run_ours(args):
     device = torch.device("cuda", local_rank)
     if world > 1:
         # Communicator set-up lines (rank, nranks, transport) go to stderr, as the record of
-        # which ranks took part; nothing of NCCL runs in the timed region.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # which ranks took part; nothing of NCCL runs in the timed region. (The environment may
+        # already set NCCL_DEBUG to VERSION, which prints only the banner.)
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,ENV")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=device)
 
