@@ -502,7 +502,7 @@ def run_ours(args):
     value = flops_step_total / (ms_step * 1e-3) / 1e12
     peak, peak_src = measured_peak()
     sustained = measured_sustained_peak()
-    # Dominant (only) kernel: the row-pair kernel fa_fwd_kernel<128, false>; per-launch algorithmic
+    # Dominant (only) kernel: the row-pair kernel fa_fwd_kernel<128, false, false>; per-launch algorithmic
     # FLOPs / mean launch time.
     achieved = (flops_dense_local + flops_causal_local) / ((dense_ms + causal_ms) * 1e-3) / 1e12
     traffic = profile_traffic()
@@ -629,7 +629,7 @@ def run_ours(args):
                      # "clocks"); cuBLAS measured under the same cap:
                      "sustained_peak": sustained,
                      "frac_vs_sustained": None if sustained is None else achieved / sustained,
-                     "kernel": "fa_sm100::fa_fwd_kernel<128, false>",
+                     "kernel": "fa_sm100::fa_fwd_kernel<128, false, false>",
                      "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
                      "traffic_note": None if traffic is None else traffic.get("note")},
         "cpu_baseline": cpu,
