@@ -453,6 +453,9 @@ def run_ours(args):
     status, word = device_status()
     if status != 0:
         raise RuntimeError(f"device status {status} ({word:#x}) after warm-up")
+    # The first collective sets up the NCCL communicator (about a second at 8 ranks). Done here,
+    # before the soak, it cannot leave the GPUs idle between the soak and the timed steps.
+    barrier()
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -462,13 +465,35 @@ def run_ours(args):
         # the timed steps run in the power-limited steady state at every N. Without it a rank's
         # share of the timed steps can be shorter than the power limit's response (at N=8 the
         # timed region is ~60 ms), and N would compare burst clocks against capped ones.
+        # The soak has to keep the GPU as busy as the timed steps do. It therefore keeps one batch
+        # of ~50 ms of steps queued behind the one running, and waits for the older batch only.
+        # Synchronising every few steps would leave the GPU idle while the host catches up: with
+        # 8 ranks on one host that was 11 % of the soak at N=8, and the GPU then stayed below its
+        # power limit.
+        # Every rank runs the same number of soak steps (from the slowest rank's estimate), so
+        # that the ranks finish the soak together and the barrier before the timed steps is
+        # short: an idle gap there lets the clock return to its maximum before the timing starts.
         soak_steps = 0
         t_soak = time.monotonic()
-        while time.monotonic() - t_soak < args.soak_s:
+        if args.soak_s > 0:
             step()
-            soak_steps += 1
-            if soak_steps % 2 == 0:
-                torch.cuda.synchronize()
+            step()
+            torch.cuda.synchronize()
+            soak_steps = 2
+            per_step = max((time.monotonic() - t_soak) / 2, 1e-5)
+            total, batch = max_over_ranks([float(args.soak_s / per_step), float(max(1, int(0.05 / per_step)))])
+            total, batch = int(total), int(batch)
+            pending = None
+            while soak_steps < total:
+                n_batch = min(batch, total - soak_steps)
+                for _ in range(n_batch):
+                    step()
+                soak_steps += n_batch
+                queued = torch.cuda.Event()
+                queued.record(stream)
+                if pending is not None:
+                    pending.synchronize()
+                pending = queued
         torch.cuda.synchronize()
         soak_s = time.monotonic() - t_soak
         barrier()
@@ -618,8 +643,10 @@ def run_ours(args):
                    "parallelism": f"slab-sharded x{world} (batch*heads split, no collective)",
                    "l2": "inputs larger than L2 (3 GiB of Q/K/V + 1 GiB O per forward)"},
         "soak": {"seconds": soak_s, "steps": soak_steps,
-                 "note": "untimed steps after the warm-up so that every N is timed at the power-limited "
-                         "steady-state clock (rank 0's figures)"},
+                 "gpu_busy": (min(1.0, soak_steps * (total_ms / args.steps) * 1e-3 / soak_s) if soak_s > 0 else None),
+                 "note": "untimed steps after the warm-up, kept queued back to back, so that every N is "
+                         "timed at the power-limited steady-state clock (rank 0's figures; gpu_busy = "
+                         "soak steps x the timed step time / soak wall time)"},
         "pct_of_bf16_peak": 100.0 * value / world / peak,
         "dense_tflops": (flops_dense_local * world / (dense_ms_max * 1e-3) / 1e12) if 0 in masks else None,
         "causal_tflops": (flops_causal_local * world / (causal_ms_max * 1e-3) / 1e12) if 1 in masks else None,
