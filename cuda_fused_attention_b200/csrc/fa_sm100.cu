@@ -80,8 +80,7 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunc
 // it; with a threshold of 8 instead, peaky rows (Q scaled by 4, config 3) made that
 // happen often enough to cost ~30 %.
 constexpr float kRescaleThreshold = 16.0f;
-constexpr uint32_t kTmemCols = 512;      // row-pair kernel: S0 | S1 | O0 | O1
-constexpr uint32_t kTmemColsOne = 256;   // one-tile kernel: S0 | O0
+constexpr uint32_t kTmemCols = 512;      // row pairs: S0 | S1 | O0 | O1; one tile: S(even j) | S(odd j) | O0
 
 constexpr int kSubBytes = kBlockM * 128;    // one 128-row x 64-element bf16 swizzle block (16 KB)
 constexpr int kMaxChunks = 64;              // key-range split: chunks per unit at most
@@ -329,10 +328,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    // Tensor memory: S0 | S1 | O0 | O1, or S0 | O0 in the one-tile kernel.
-    constexpr uint32_t kCols = kOneTile ? kTmemColsOne : kTmemCols;
-    constexpr uint32_t kColO0 = kOneTile ? kBlockN : C::kColO0;
-    static_assert(!kOneTile || kColO0 + D <= kTmemColsOne, "one-tile TMEM budget");
+    // Tensor memory: S0 | S1 | O0 | O1. The one-tile kernel uses S0 and S1 as a double buffer
+    // (key tile j in S_(j & 1)), so that QK^T of the next key tile runs during the softmax.
+    constexpr uint32_t kCols = kTmemCols;
+    constexpr uint32_t kColO0 = C::kColO0;
 
     // ---- work item ---------------------------------------------------------------
     // A unit is a row pair (256 rows, two Q tiles) of one slab, or in the one-tile kernel a
@@ -546,35 +545,41 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                     }
                 }
             } else {
-                // One Q tile (tile 0 only): the same pipeline without tile 1's MMAs.
+                // One Q tile, S double-buffered: key tile j in S_(j & 1). QK^T(j+1) is issued before
+                // the PV of tile j waits for its P, so it runs while the softmax works on tile j. The
+                // P barriers are per buffer (kBarPHalf/kBarPFull + b, phase (j >> 1) & 1): the softmax
+                // can finish tile j + 1 before this thread waits for tile j's P, never tile j + 2,
+                // whose S is issued only after that wait. kBarPvHalf + 1 completes when tile j's PV
+                // has: the softmax waits on it before it rescales O for tile j + 1.
                 if (ok) {
                     tc_fence_after();
                     issue_qk<D>(t_s0, sq0, slot_addr(0));
                     umma_commit(bar(C::kBarSFull + 0));
                     umma_commit(empty_bar(0));
                 }
+                uint32_t t_sj = t_s0;                 // S of key tile j; the other buffer is t_sj ^ kBlockN
                 for (int j = 0; ok && j < n_kv; ++j) {
                     const int vi = 2 * j + 1;
-                    const int ki = 2 * j + 2;
-                    const bool more = j + 1 < n_kv;
-                    const uint32_t par = static_cast<uint32_t>(j & 1);
-                    if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
-                    if (!wait_bounded(bar(C::kBarPHalf + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
-                    tc_fence_after();
-                    issue_pv<D, 0, 4>(t_o0, t_s0, slot_addr(vi), j > 0);
-                    umma_commit(bar(C::kBarPvHalf + 0));
-                    if (!wait_bounded(bar(C::kBarPFull + 0), par, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
-                    tc_fence_after();
-                    issue_pv<D, 4, 8>(t_o0, t_s0, slot_addr(vi), true);
-                    umma_commit(empty_bar(vi));
-                    if (!more) umma_commit(bar(C::kBarOFull + 0));
-                    if (more) {
+                    if (j + 1 < n_kv) {
+                        const int ki = vi + 1;
                         if (!wait_bounded(full_bar(ki), full_par(ki), abort_flag, timeout, kSiteMmaK)) { ok = false; break; }
                         tc_fence_after();
-                        issue_qk<D>(t_s0, sq0, slot_addr(ki));
-                        umma_commit(bar(C::kBarSFull + 0));
+                        issue_qk<D>(t_sj ^ kBlockN, sq0, slot_addr(ki));
+                        umma_commit(bar(C::kBarSFull + ((j + 1) & 1)));
                         umma_commit(empty_bar(ki));
                     }
+                    if (!wait_bounded(full_bar(vi), full_par(vi), abort_flag, timeout, kSiteMmaV)) { ok = false; break; }
+                    if (!wait_bounded(bar(C::kBarPHalf + (j & 1)), (j >> 1) & 1, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 0, 4>(t_o0, t_sj, slot_addr(vi), j > 0);
+                    umma_commit(bar(C::kBarPvHalf + 0));
+                    if (!wait_bounded(bar(C::kBarPFull + (j & 1)), (j >> 1) & 1, abort_flag, timeout, kSiteMmaP0)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv<D, 4, 8>(t_o0, t_sj, slot_addr(vi), true);
+                    umma_commit(empty_bar(vi));
+                    umma_commit(bar(C::kBarPvHalf + 1));
+                    if (j + 1 == n_kv) umma_commit(bar(C::kBarOFull + 0));
+                    t_sj ^= kBlockN;
                 }
             }
             // Every MMA issued above must finish before tensor memory is released.
@@ -589,7 +594,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const int quarter = warp % 4;              // TMEM lane quarter of this warp
         const int r = quarter * 32 + lane;         // row within the Q tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const uint32_t t_s = lane_base + (t == 0 ? C::kColS0 : C::kColS1);
+        // S of the current key tile: the Q tile's own buffer (row pairs), or S_(j & 1) in the
+        // one-tile kernel, which flips between S0 and S1 after every key tile.
+        uint32_t t_s = lane_base + (t == 0 ? C::kColS0 : C::kColS1);
+        static_assert((C::kColS0 ^ C::kColS1) == kBlockN && C::kColS0 == 0, "S buffers at columns 0 and 128");
         const uint32_t t_o = lane_base + (t == 0 ? kColO0 : C::kColO1);
         const int row = q_row0 + t * kBlockM + r;            // query index in the slab
         const int limit = p.causal ? min(row, n - 1) : n - 1;  // last key this row attends to
@@ -666,7 +674,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         };
 
         for (int j = 0; j < n_kv; ++j) {
-            ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarSFull + t), j & 1, abort_flag, timeout, kSiteSoftS));
+            // Barrier set of this key tile's S buffer: the Q tile's own (row pairs), or that of
+            // S_(j & 1) (one tile; those barriers complete once per two key tiles).
+            ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarSFull + (kOneTile ? (j & 1) : t)),
+                                                      static_cast<uint32_t>(kOneTile ? (j >> 1) & 1 : j & 1),
+                                                      abort_flag, timeout, kSiteSoftS));
             if (!ok) break;
             tc_fence_after();
 
@@ -748,10 +760,21 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 if (h == 0) {
                     // Keys 0-63 of P are final: correct O first (the PV is the next reader of O;
                     // at j = 0 it overwrites O), then hand the first half to the MMA.
-                    if (j > 0 && __any_sync(0xffffffffu, o_scale != 1.0f)) rescale_o(o_scale);
+                    if (j > 0 && __any_sync(0xffffffffu, o_scale != 1.0f)) {
+                        if constexpr (kOneTile) {
+                            // This tile's S can be ready before the previous tile's PV has
+                            // finished accumulating into O: wait for that PV first.
+                            ok = __all_sync(0xffffffffu, wait_bounded(bar(C::kBarPvHalf + 1),
+                                                                      static_cast<uint32_t>((j - 1) & 1), abort_flag,
+                                                                      timeout, kSiteSoftO));
+                            if (!ok) break;
+                            tc_fence_after();
+                        }
+                        rescale_o(o_scale);
+                    }
                     tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(bar(C::kBarPHalf + t));
+                    mbar_arrive(bar(C::kBarPHalf + (kOneTile ? (j & 1) : t)));
                 }
             }
             if (!ok) break;
@@ -760,7 +783,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             if (blockIdx.x == 0 && j == 0 && t == 0) debug_dump_p(t_s, r, 0, 2);
 #endif
             tc_fence_before();
-            mbar_arrive(bar(C::kBarPFull + t));
+            mbar_arrive(bar(C::kBarPFull + (kOneTile ? (j & 1) : t)));
+            if constexpr (kOneTile) t_s ^= kBlockN;
         }
 
         // ---- epilogue ---------------------------------------------------------
