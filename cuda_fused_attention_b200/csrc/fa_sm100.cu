@@ -1254,22 +1254,22 @@ int forward(const void* q, const void* k, const void* v, void* o, int batch, int
     // Kernel choice. A CTA normally takes a row pair (two Q tiles whose softmax phases overlap
     // on one SM). Dense: when even one CTA per Q tile would leave SMs idle, each Q tile gets its
     // own CTA instead (twice the CTAs, each with a shorter critical path). Causal: when the row
-    // pairs fit in one wave, the longest CTA sets the time, and one Q tile per CTA shortens it
-    // (measured on B200: 0.82-0.87x the row-pair time at (1,8,4096,D) and (2,8,2048,D)).
+    // pairs fit in one wave, the longest CTA sets the time, and one Q tile per CTA (S double-
+    // buffered, so its QK^T overlaps its softmax) shortens it: 0.60-0.76x the row-pair time at
+    // (1,8,2048,D), (2,8,2048,D), (1,4,8192,D) and (1,2,16384,128) (B200, CUDA-graph replay).
     const int pairs = (seq_len + kRowsPerCta - 1) / kRowsPerCta;
     const int kv_all = (seq_len + kBlockN - 1) / kBlockN;
     bool single = causal ? count * pairs <= sms : count * pairs * kQTiles <= sms;
-    // Causal key-range split (row-pair kernel only): chunks of split_len key tiles. A one-wave
-    // causal grid lasts as long as its heaviest row pair; splitting the heavy pairs' key ranges
-    // pays for its partials and merges where the grid is small (at most half a wave of pairs) or
-    // the rows are long (64 key tiles or more). Measured on B200 (CUDA-graph replay) against one
-    // Q tile per CTA: (1,8,2048,64) 26.6 -> 23.2 us in chunks of a third of the key tiles;
-    // (1,4,8192,128) 108.2 -> 87.2 us, (1,2,16384,128) 211.5 -> 156.2 us and (1,1,32768,128)
-    // 418.4 -> 295.5 us in halves; at (2,8,2048,D), (4,8,1024,D) and (1,16,2048,64) (a full wave
-    // of pairs with short rows) the split was slower.
+    // Causal key-range split (row-pair kernel only): chunks of split_len key tiles. Against one Q
+    // tile per CTA it pays only for very long rows in a grid whose row pairs fit in one wave:
+    // (1,1,32768,128) 296.1 -> 265.5 us in chunks of a sixth of the key tiles (halves: 295.6 us).
+    // At D = 64, and up to 128 key tiles at D = 128, the one-tile kernel was faster than every
+    // chunk length measured: (1,1,32768,64) 244.9 us against 266.1, (1,8,2048,D) 19.6 / 22.6
+    // against 22.2 / 26.9, (1,4,8192,D) 64.4 / 74.8 against 86.3 / 89.4, (1,2,16384,128) 147.2
+    // against 153.5.
     int split_len = 0;
-    if (causal && count * pairs <= sms && kv_all >= 16 && (2 * count * pairs <= sms || kv_all >= 64)) {
-        split_len = kv_all >= 64 ? (kv_all + 1) / 2 : (kv_all + 2) / 3;
+    if (causal && head_dim == 128 && count * pairs <= sms && kv_all >= 256) {
+        split_len = (kv_all + 5) / 6;
         single = false;
     }
     if (t_forced_split >= 0) split_len = t_forced_split;
