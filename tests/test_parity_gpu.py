@@ -385,3 +385,14 @@ def test_one_tile_kernel_equals_row_pair_kernel(oracle, cuda_device):
     finally:
         lib.fa_sm100_test_force_kernel(0)
         lib.fa_sm100_test_force_split(-1)
+
+
+@pytest.mark.parametrize("b, h, n, d, causal", [(1, 1, 32768, 128, 1), (1, 1, 32768, 64, 1), (1, 2, 16384, 128, 1),
+                                                (1, 1, 32768, 128, 0)])
+def test_long_rows_sampled(oracle, cuda_device, b, h, n, d, causal):
+    """Long rows in a grid of few slabs, where the launcher's choice differs: (1,1,32768,128)
+    causal splits each row pair's 256 key tiles into chunks of a sixth (partials merged in chunk
+    order); (1,1,32768,64) and (1,2,16384,128) causal run one Q tile per CTA through 256 and 128
+    key tiles (S double-buffered); (1,1,32768,128) dense runs 128 row-pair CTAs. Sampled rows
+    against the FP64 oracle, the reference's own generator."""
+    _sampled_case(oracle, cuda_device, b, h, n, d, causal, 0, "reference")
