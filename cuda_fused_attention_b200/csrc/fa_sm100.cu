@@ -8,8 +8,11 @@
 //
 //   * One CTA owns 256 query rows of one (batch, head) slab, as two 128-row Q
 //     tiles that ping-pong between two softmax warpgroups. When a grid of such
-//     CTAs would fill less than half the GPU, each CTA takes a single Q tile
-//     (the second warpgroup idles), doubling the CTAs and shortening the path.
+//     CTAs would fill less than half the GPU (dense), or the row pairs fit in one
+//     wave (causal), each CTA takes a single Q tile (the second warpgroup idles)
+//     with S double-buffered in tensor memory, so that the next key tile's QK^T
+//     runs during the softmax. Causal launches with very long rows and few slabs
+//     split each row pair's key range across CTAs and merge the partial results.
 //   * QK^T and PV are tcgen05.mma (kind::f16, M=128, N=128 / N=D, BF16 in,
 //     FP32 accumulate) issued by one thread of the MMA warp. S and O live in
 //     tensor memory: S0 | S1 | O0 | O1 = 512 columns at D=128.
