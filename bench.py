@@ -172,61 +172,28 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU legs
-SAMPLE_ROWS = 512    # query rows per host thread per mask in one reference-arm step
-CPU_BASELINE_REPEATS = 4   # the GPU arm's cpu_baseline: this many reference-arm step samples
-
-
-def sample_rows(seq_len, rows, thread, threads):
-    """Query-row ranges of one host thread's share of the sample, dense and causal.
-
-    Dense: `rows` consecutive rows. Causal: two mirrored halves [a, a + rows/2) and
-    [N - a - rows/2, N - a), so that row r and row N-1-r (r+1 and N-r keys) pair up and every
-    thread's causal share is rows*(N+1)/2 query-key pairs, the mean of a causal slab. The
-    offset a spreads the threads over the first half of the slab."""
-    half = rows // 2
-    span = max(0, seq_len // 2 - half)
-    a = (thread * span) // max(1, threads)
-    dense = [(a, min(seq_len, a + rows))]
-    causal = [(a, a + half), (seq_len - a - half, seq_len - a)]
-    return dense, causal
-
-
-def pairs_in(ranges, seq_len, causal):
-    """Query-key pairs the oracle evaluates for the given row ranges."""
-    total = 0
-    for lo, hi in ranges:
-        if causal:
-            total += (hi * (hi + 1) - lo * (lo + 1)) // 2   # rows r in [lo, hi) see r+1 keys
-        else:
-            total += (hi - lo) * seq_len
-    return total
-
-
-def cpu_row_sample(threads, seq_len, head_dim, rows=SAMPLE_ROWS):
-    """One bounded, balanced sample of the workload on the host: every thread computes the same
-    amount of dense and causal work (sample_rows) of one (seq_len x head_dim) slab with the oracle
-    port (oracle/fa_oracle.cpp, the reference's reference_attention restated statement for
-    statement and pinned to it bit for bit). Returns (flops, seconds)."""
+def cpu_slab_step(threads, seq_len, head_dim, causal):
+    """One bounded, balanced sample of the workload on the host: every host thread computes one
+    whole (seq_len x head_dim) slab with the same mask, so no thread idles while another
+    finishes. The function timed is the reference's own reference_attention
+    (benchmarks/bench_flash_attention.cu:105-145), compiled from its sources into oracle/_ref;
+    where that library is absent, the oracle port pinned to it bit for bit
+    (oracle/fa_oracle.cpp). Returns (flops, seconds, kind) with kind "reference" or "port"."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import fa_oracle
-    lib = fa_oracle.load()
+    ref = fa_oracle.load_reference()
+    fn, kind = (ref.ref_reference_attention, "reference") if ref is not None else \
+        (fa_oracle.load().fa_oracle_attention, "port")
     q, k, v = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
-    # A private copy of the slab per thread, so no two threads share cache lines.
+    # A private copy of the slab and its output per thread, so no two threads share cache lines.
     slabs = [tuple(np.copy(x) for x in (q, k, v)) for _ in range(threads)]
+    outs = [np.empty(seq_len * head_dim, np.float64) for _ in range(threads)]
     P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
-    plans = [sample_rows(seq_len, rows, i, threads) for i in range(threads)]
-    flops = 0.0
-    for dense, causal in plans:
-        flops += 4.0 * head_dim * (pairs_in(dense, seq_len, False) + pairs_in(causal, seq_len, True))
 
     def work(i):
         q_, k_, v_ = slabs[i]
-        dense, causal = plans[i]
-        for ranges, mask in ((dense, 0), (causal, 1)):
-            for lo, hi in ranges:
-                out = np.empty((hi - lo) * head_dim, np.float64)
-                lib.fa_oracle_attention_rows(P(q_), P(k_), P(v_), P(out), seq_len, head_dim, mask, 0, lo, hi)
+        fn(P(q_), P(k_), P(v_), P(outs[i]), 1, 1, seq_len, head_dim, int(causal))
 
     pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
     t0 = time.perf_counter()
@@ -234,42 +201,25 @@ def cpu_row_sample(threads, seq_len, head_dim, rows=SAMPLE_ROWS):
         t.start()
     for t in pool:
         t.join()
-    return flops, time.perf_counter() - t0
+    seconds = time.perf_counter() - t0
+    flops = threads * fa_oracle.attention_flops(1, 1, seq_len, head_dim, causal)
+    return flops, seconds, kind
 
 
-def cpu_port_vs_reference(threads, seq_len=1024, head_dim=128):
-    """The port's throughput against the reference's own reference_attention (compiled from its
-    sources into oracle/_ref) on the same whole slabs, one dense and one causal per thread:
-    {"reference_tflops", "port_tflops", "port_over_reference"}, or None without oracle/_ref."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import numpy as np
-    import fa_oracle
-    ref = fa_oracle.load_reference()
-    if ref is None:
-        return None
-    lib = fa_oracle.load()
-    q, k, v = fa_oracle.make_inputs(1, 1, seq_len, head_dim)
-    slabs = [tuple(np.copy(x) for x in (q, k, v)) for _ in range(threads)]
-    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
-    flops = threads * sum(fa_oracle.attention_flops(1, 1, seq_len, head_dim, c) for c in (0, 1))
-
-    def timed(fn):
-        def work(i):
-            out = np.empty(seq_len * head_dim, np.float64)
-            for causal in (0, 1):
-                fn(P(slabs[i][0]), P(slabs[i][1]), P(slabs[i][2]), P(out), 1, 1, seq_len, head_dim, causal)
-        pool = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
-        t0 = time.perf_counter()
-        for t in pool:
-            t.start()
-        for t in pool:
-            t.join()
-        return flops / (time.perf_counter() - t0) / 1e12
-
-    reference = timed(ref.ref_reference_attention)
-    port = timed(lib.fa_oracle_attention)
-    return {"shape": [1, 1, seq_len, head_dim], "masks": "dense+causal", "threads": threads,
-            "reference_tflops": reference, "port_tflops": port, "port_over_reference": port / reference}
+def cpu_sample(threads, steps, seq_len, head_dim):
+    """`steps` reference-arm steps, dense and causal alternating (dense first):
+    {"tflops", "flops", "seconds", "kind", "per_mask"}."""
+    flops = secs = 0.0
+    kind = None
+    per_mask = {"dense": [], "causal": []}
+    for step in range(steps):
+        causal = step % 2
+        f, s_, kind = cpu_slab_step(threads, seq_len, head_dim, causal)
+        flops += f
+        secs += s_
+        per_mask["causal" if causal else "dense"].append(f / s_ / 1e12)
+    return {"tflops": flops / secs / 1e12, "flops": flops, "seconds": secs, "kind": kind,
+            "per_mask": {m: spread(r) for m, r in per_mask.items() if r}}
 
 
 def cpu_single_thread_configs():
@@ -322,19 +272,16 @@ def run_reference_arm(args):
         return 0   # the CPU reference runs once, on rank 0
     threads = host_threads()
     n, d = CONFIG["seq_len"], CONFIG["head_dim"]
-    for _ in range(args.warmup):   # warm-up on a reduced sample: the CPU has nothing to warm
-        cpu_row_sample(threads, n, d, rows=32)
-    flops = secs = 0.0
-    rates = []
-    for _ in range(args.steps):
-        f, s_ = cpu_row_sample(threads, n, d)
-        flops += f
-        secs += s_
-        rates.append(f / s_ / 1e12)
-    value = flops / secs / 1e12
-    sample = (f"per step and host thread: {SAMPLE_ROWS} dense + {SAMPLE_ROWS} causal query rows (mirrored "
-              f"halves, mean causal cost) of one (N=8192, D=128) slab, the same work on every thread; "
-              f"oracle port of reference_attention (bench_flash_attention.cu:105-145); warm-up steps 32 rows")
+    for step in range(args.warmup):   # warm-up on (1024 x D) slabs: the CPU has nothing to warm
+        cpu_slab_step(threads, 1024, d, step % 2)
+    sample = cpu_sample(threads, args.steps, n, d)
+    value = sample["tflops"]
+    secs = sample["seconds"]
+    function = ("the reference's own reference_attention (bench_flash_attention.cu:105-145) from oracle/_ref"
+                if sample["kind"] == "reference" else "the oracle port of reference_attention (no oracle/_ref)")
+    description = (f"per step: every host thread computes one whole (N={n}, D={d}) slab, all threads the same "
+                   f"mask, dense and causal alternating between steps; {function}; warm-up steps on "
+                   f"(1024 x {d}) slabs")
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
@@ -342,9 +289,8 @@ def run_reference_arm(args):
         "data": "synthetic N(0,1) bf16 (reference generator, seeds 11/22/33)",
         "impl": "reference",
         "config": {"workload": "BASELINE config 5 (16,32,8192,128) dense+causal, CPU sample", **CONFIG},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample,
-                         "spread_over_steps": spread(rates),
-                         "port_vs_reference": cpu_port_vs_reference(threads),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": sample["kind"],
+                         "sample": description, "spread_over_steps": sample["per_mask"],
                          "extrapolated": cpu_extrapolation(value),
                          "single_thread": cpu_single_thread_configs()},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -608,23 +554,17 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        # The reference arm's step sample (the same rows, the same threads), repeated.
+        # The reference arm's first two steps: one dense and one causal whole slab per host thread.
         threads = host_threads()
-        flops = secs = 0.0
-        rates = []
-        for _ in range(CPU_BASELINE_REPEATS):
-            f, s_ = cpu_row_sample(threads, n, d)
-            flops += f
-            secs += s_
-            rates.append(f / s_ / 1e12)
-        cpu = {"value": flops / secs / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"{CPU_BASELINE_REPEATS} x the reference arm's step sample: {SAMPLE_ROWS} dense + "
-                         f"{SAMPLE_ROWS} causal query rows (mirrored halves, mean causal cost) of one ({n} x {d}) "
-                         f"slab per host thread, the same work on every thread, oracle port of reference_attention; "
-                         f"{secs:.1f} s wall",
-               "spread_over_repeats": spread(rates),
-               "port_vs_reference": cpu_port_vs_reference(threads),
-               "extrapolated": cpu_extrapolation(flops / secs / 1e12),
+        sample = cpu_sample(threads, 2, n, d)
+        cpu = {"value": sample["tflops"], "unit": "TFLOP/s", "cores": threads, "kind": sample["kind"],
+               "sample": f"the reference arm's first two steps: every host thread computes one whole ({n} x {d}) "
+                         f"slab dense, then one causal; "
+                         + ("the reference's own reference_attention from oracle/_ref"
+                            if sample["kind"] == "reference" else "the oracle port of reference_attention")
+                         + f"; {sample['seconds']:.1f} s wall",
+               "per_mask": sample["per_mask"],
+               "extrapolated": cpu_extrapolation(sample["tflops"]),
                "single_thread": cpu_single_thread_configs()}
 
     if world > 1:

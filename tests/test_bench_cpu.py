@@ -53,22 +53,21 @@ def test_clock_summary_parses_samples():
     assert back["sm_mhz"] == 1605 and back["reasons"] == ["sw_power_cap"] and back["samples"] == 3
 
 
-def test_cpu_sample_gives_every_thread_the_same_work():
-    """Each host thread's share: `rows` dense rows and `rows` causal rows whose key counts average
-    to a causal slab's mean (N+1)/2, so no thread idles while another finishes."""
+def test_cpu_step_gives_every_thread_a_whole_slab_of_one_mask():
+    """A reference-arm step: every host thread one whole slab with the same mask (so no thread
+    idles while another finishes); flops counted with the reference's FLOP formula; the
+    reference's own function when oracle/_ref is built."""
     bench = _bench()
-    for n, rows, threads in ((8192, 1024, 16), (8192, 2048, 7), (1024, 64, 3)):
-        loads = set()
-        for t in range(threads):
-            dense, causal = bench.sample_rows(n, rows, t, threads)
-            assert all(0 <= lo < hi <= n for lo, hi in dense + causal)
-            # pairs_in against a direct count
-            direct_causal = sum(r + 1 for lo, hi in causal for r in range(lo, hi))
-            assert bench.pairs_in(causal, n, True) == direct_causal
-            assert bench.pairs_in(dense, n, False) == sum(hi - lo for lo, hi in dense) * n
-            assert direct_causal * 2 == rows * (n + 1)
-            loads.add((bench.pairs_in(dense, n, False), direct_causal))
-        assert len(loads) == 1
+    import fa_oracle
+    for causal in (0, 1):
+        flops, seconds, kind = bench.cpu_slab_step(3, 256, 64, causal)
+        assert flops == 3 * fa_oracle.attention_flops(1, 1, 256, 64, causal)
+        assert seconds > 0
+        assert kind == ("reference" if fa_oracle.load_reference() is not None else "port")
+    sample = bench.cpu_sample(2, 3, 128, 64)
+    assert sample["flops"] == 2 * (2 * fa_oracle.attention_flops(1, 1, 128, 64, 0) +
+                                   fa_oracle.attention_flops(1, 1, 128, 64, 1))
+    assert set(sample["per_mask"]) == {"dense", "causal"}
 
 
 def test_slab_ranges_cover_every_slab_once():
