@@ -144,12 +144,25 @@ def _sampled_rows(n, slabs):
     return picks
 
 
+# The reference generator's inputs of the last sampled shape: config 5 has 1.6e9 values (tens of
+# seconds on the host), generated once for its dense and its causal test.
+_REFERENCE_INPUTS = {}
+
+
+def _reference_inputs(oracle, b, h, n, d, family):
+    key = (b, h, n, d, family)
+    if key not in _REFERENCE_INPUTS:
+        _REFERENCE_INPUTS.clear()
+        _REFERENCE_INPUTS[key] = oracle.make_inputs(b, h, n, d, family)
+    return _REFERENCE_INPUTS[key]
+
+
 def _sampled_case(oracle, cuda_device, b, h, n, d, causal, family, generator):
     import torch
     from cuda_fused_attention_b200 import AttentionShape
     shape = AttentionShape(b, h, n, d)
     if generator == "reference":
-        q, k, v = oracle.make_inputs(b, h, n, d, family)
+        q, k, v = _reference_inputs(oracle, b, h, n, d, family)
         dq, dk, dv = _to_dev(q, cuda_device), _to_dev(k, cuda_device), _to_dev(v, cuda_device)
     else:   # seeded torch N(0,1) -> bf16 on the device (configs too large for the CPU generator)
         g = torch.Generator(device=cuda_device)
@@ -189,13 +202,13 @@ def test_config3_sampled(oracle, cuda_device):
 
 def test_config4_sampled(oracle, cuda_device):
     """(1,32,16384,128) causal, long context."""
-    _sampled_case(oracle, cuda_device, 1, 32, 16384, 128, 1, 0, "torch")
+    _sampled_case(oracle, cuda_device, 1, 32, 16384, 128, 1, 0, "reference")
 
 
 @pytest.mark.parametrize("causal", [0, 1])
 def test_config5_sampled(oracle, cuda_device, causal):
     """(16,32,8192,128) dense and causal."""
-    _sampled_case(oracle, cuda_device, 16, 32, 8192, 128, causal, 0, "torch")
+    _sampled_case(oracle, cuda_device, 16, 32, 8192, 128, causal, 0, "reference")
 
 
 @pytest.mark.parametrize("causal", [0, 1])
