@@ -63,7 +63,7 @@ typedef struct FaTilingInfo {
  * Replaces launch_attention_tensorcore_v3 (include/flash_attention.h:92,
  * kernels/v3/v3_tensorcore.cu:722-750). q, k, v, o: device pointers, 16-byte
  * aligned, each batch*heads*seq_len*head_dim bf16 elements. Every element of o
- * is written. A causal launch with few (batch, head) slabs and long rows may
+ * is written. o may be q (O written over Q) and k may be v. A causal launch with few (batch, head) slabs and long rows may
  * split the key range of its heaviest row pairs across several CTAs; such a
  * launch takes its workspace (partials of the split rows) from a memory pool
  * of the library, allocated and freed in order on `stream` (stream-ordered

@@ -409,3 +409,38 @@ def test_long_rows_sampled(oracle, cuda_device, b, h, n, d, causal):
     key tiles (S double-buffered); (1,1,32768,128) dense runs 128 row-pair CTAs. Sampled rows
     against the FP64 oracle, the reference's own generator."""
     _sampled_case(oracle, cuda_device, b, h, n, d, causal, 0, "reference")
+
+
+@pytest.mark.parametrize("kernel, split, b, h, n, causal", [(1, 0, 1, 2, 700, 1), (2, 0, 2, 3, 700, 0),
+                                                             (2, 3, 1, 2, 2048, 1)])
+def test_in_place_output_and_shared_k_v(oracle, cuda_device, kernel, split, b, h, n, causal):
+    """O written over Q (each Q tile is read by one CTA, before it writes the same rows of O; with
+    the key-range split the merging chunk stores only after every other chunk of its rows has
+    published), and one tensor passed as both K and V: the same bits as separate buffers, for
+    one Q tile per CTA, row pairs, and row pairs with the key range split."""
+    import torch
+    from cuda_fused_attention_b200 import AttentionShape, _lib, launch_attention_sm100
+    lib = _lib.load()
+    d = 128
+    q, k, _ = oracle.make_inputs(b, h, n, d)
+    shape = AttentionShape(b, h, n, d)
+    assert lib.fa_sm100_test_force_kernel(kernel) == 0 and lib.fa_sm100_test_force_split(split) == 0
+    try:
+        dq, dk = _to_dev(q, cuda_device), _to_dev(k, cuda_device)
+        dkv = dk.clone()                        # V = K, as its own buffer
+        separate = _poisoned_like(dq)
+        launch_attention_sm100(dq, dk, dkv, separate, shape, causal)
+        shared = _poisoned_like(dq)
+        launch_attention_sm100(dq, dk, dk, shared, shape, causal)          # K and V: one tensor
+        in_place = dq.clone()
+        launch_attention_sm100(in_place, dk, dk, in_place, shape, causal)  # O over Q
+        torch.cuda.synchronize()
+    finally:
+        lib.fa_sm100_test_force_split(-1)
+        lib.fa_sm100_test_force_kernel(0)
+    check_device_clean()
+    want = _to_host_bits(separate)
+    assert np.array_equal(_to_host_bits(shared), want)
+    assert np.array_equal(_to_host_bits(in_place), want)
+    ref = oracle.attention(q, k, k, b, h, n, d, causal)
+    assert oracle.compare(want, ref, d, 2.0)["passed"]
