@@ -444,3 +444,17 @@ def test_in_place_output_and_shared_k_v(oracle, cuda_device, kernel, split, b, h
     assert np.array_equal(_to_host_bits(in_place), want)
     ref = oracle.attention(q, k, k, b, h, n, d, causal)
     assert oracle.compare(want, ref, d, 2.0)["passed"]
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_tensors_past_2_31_elements(oracle, cuda_device, causal):
+    """(65,32,8192,128): 2.18e9 elements per tensor (4.4 GB each). The last slab starts past 2^31
+    elements, so a 32-bit index or offset anywhere on the path (tensor maps, slab coordinates,
+    work-item decode) would show as a wrong or unwritten last slab. Sampled rows of the first,
+    middle and last slab against the FP64 oracle; no element left unwritten (seeded torch inputs
+    on the device)."""
+    import torch
+    free, _ = torch.cuda.mem_get_info()
+    if free < 24 << 30:
+        pytest.skip("needs 24 GiB of free device memory")
+    _sampled_case(oracle, cuda_device, 65, 32, 8192, 128, causal, 0, "torch")
