@@ -122,6 +122,23 @@ def _check_tensor(name, t, shape):
         raise ValueError(f"{name} has {t.numel()} elements, shape needs {shape.numel}")
 
 
+def _device_of(*tensors):
+    """The one CUDA device of the tensor arguments (None if all are raw pointers)."""
+    devices = {t.device for t in tensors if not isinstance(t, int)}
+    if len(devices) > 1:
+        raise ValueError(f"q, k, v and o must be on one device, got {sorted(str(d) for d in devices)}")
+    return devices.pop() if devices else None
+
+
+def _on_device(device):
+    """Make `device` current for the call: the C entry points launch on the current device."""
+    import contextlib
+    if device is None:
+        return contextlib.nullcontext()
+    import torch
+    return torch.cuda.device(device)
+
+
 def launch_attention_sm100(q, k, v, o, shape, causal=False, stream=None):
     """Counterpart of launch_attention_tensorcore_v3 (include/flash_attention.h:92).
 
@@ -131,9 +148,10 @@ def launch_attention_sm100(q, k, v, o, shape, causal=False, stream=None):
     """
     for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
         _check_tensor(name, t, shape)
-    status = _lib.load().fa_sm100_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), shape.batch, shape.heads,
-                                      shape.seq_len, shape.head_dim, 1 if causal else 0,
-                                      _stream_handle(stream, q))
+    with _on_device(_device_of(q, k, v, o)):
+        status = _lib.load().fa_sm100_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), shape.batch, shape.heads,
+                                          shape.seq_len, shape.head_dim, 1 if causal else 0,
+                                          _stream_handle(stream, q))
     _check(status, "fa_sm100_fwd")
 
 
@@ -141,9 +159,10 @@ def launch_attention_sm100_slabs(q, k, v, o, shape, causal, slab_begin, slab_end
     """Forward over slabs [slab_begin, slab_end) of batch*heads (one GPU's shard)."""
     for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
         _check_tensor(name, t, shape)
-    status = _lib.load().fa_sm100_fwd_slabs(_ptr(q), _ptr(k), _ptr(v), _ptr(o), shape.batch, shape.heads,
-                                            shape.seq_len, shape.head_dim, 1 if causal else 0,
-                                            int(slab_begin), int(slab_end), _stream_handle(stream, q))
+    with _on_device(_device_of(q, k, v, o)):
+        status = _lib.load().fa_sm100_fwd_slabs(_ptr(q), _ptr(k), _ptr(v), _ptr(o), shape.batch, shape.heads,
+                                                shape.seq_len, shape.head_dim, 1 if causal else 0,
+                                                int(slab_begin), int(slab_end), _stream_handle(stream, q))
     _check(status, "fa_sm100_fwd_slabs")
 
 

@@ -118,3 +118,19 @@ def test_python_wrapper_rejects_bad_tensors():
     b = torch.zeros(8 * 64, dtype=torch.bfloat16)
     with pytest.raises(TypeError):   # CPU tensor: no silent CPU path
         launch_attention_sm100(b, b, b, b, shape)
+
+
+def test_python_wrapper_requires_one_device():
+    """The C entry points launch on the current device: the Python wrapper makes the tensors'
+    device current, and rejects arguments spread over two devices before any CUDA call."""
+    import torch
+    from cuda_fused_attention_b200 import _device_of
+
+    class Fake:
+        def __init__(self, device):
+            self.device = torch.device(device)
+
+    assert _device_of(Fake("cuda:1"), Fake("cuda:1"), 1234, Fake("cuda:1")) == torch.device("cuda:1")
+    assert _device_of(1, 2, 3, 4) is None
+    with pytest.raises(ValueError, match="one device"):
+        _device_of(Fake("cuda:0"), Fake("cuda:1"), Fake("cuda:0"), Fake("cuda:0"))
